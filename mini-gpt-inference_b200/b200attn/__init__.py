@@ -1,0 +1,16 @@
+"""b200attn -- sm_100a paged-attention backend for the minivllm runtime.
+
+Public API (CUDA only, no fallback):
+  paged_attention_batch_b200  -- batched paged decode attention (+ fused KV write)
+  kv_scatter_b200             -- slot-mapping KV-cache scatter
+  chunked_prefill_b200        -- prefix-aware chunked-prefill attention
+  chunked_prefill_batch_b200  -- several prefill chunks in one launch
+"""
+from .ops import (chunked_prefill_b200, chunked_prefill_batch_b200, decode_bytes,
+                  is_available, kv_scatter_b200, paged_attention_batch_b200)
+from ._lib import LIB_PATH, load as load_library
+
+__all__ = [
+    "paged_attention_batch_b200", "kv_scatter_b200", "chunked_prefill_b200",
+    "chunked_prefill_batch_b200", "decode_bytes", "is_available", "load_library", "LIB_PATH",
+]

@@ -1,0 +1,25 @@
+// kernels.h -- launcher entry points of the device kernels (host side).
+// Arguments arrive already validated by capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b200_paged_attn.h"
+
+namespace b200 {
+
+using DecodeLaunch = b200_decode_args_t;
+
+int launch_paged_decode(const DecodeLaunch& a, cudaStream_t stream);
+int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream);
+// tcgen05 prefill over `n` sequences sharing one pool (bf16, D in {64,128}).
+int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream);
+bool prefill_tc_supported(const b200_prefill_args_t& a);
+
+// Split-K planning shared by the launcher and the workspace query.
+int64_t decode_tiles_per_split(int64_t units, int64_t max_tiles, int32_t hint, int num_sms);
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t D, int64_t M, int64_t S,
+                              int32_t hint, size_t es, int num_sms);
+
+}  // namespace b200

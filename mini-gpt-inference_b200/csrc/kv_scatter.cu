@@ -1,0 +1,171 @@
+// kv_scatter.cu -- slot-mapping KV-cache scatter.
+//
+// For every token n the H*D elements of k[n] (and v[n]) are stored as one
+// contiguous run at pool[layer, slot[n] / S, slot[n] % S, :, :].  The pool run
+// is contiguous, so the kernel writes it with 16-byte vector stores; source
+// rows are read with 16-byte loads when their innermost stride is 1 and
+// aligned, else element by element (q/k/v arrive as strided views of the
+// fused QKV projection, minivllm/attention.py:180-191 and :360-368).
+// Semantics: minivllm/attention.py:370-392 (decode) and :193-208 via
+// KVBlockPool.write_layer (minivllm/kv_block_pool.py:91-109) (prefill).
+#include "common.cuh"
+#include "host_util.h"
+#include "kernels.h"
+
+namespace b200 {
+
+struct ScatterParams {
+  int64_t N, H, D, S, P;
+  int64_t layer_row0;  // layer * P * S
+  const void* k;
+  const void* v;
+  int64_t ks0, ks1, ks2, vs0, vs1, vs2;
+  int32_t in_dtype;
+  void* kp;
+  void* vp;
+  int32_t pool_dtype;
+  const void* slots;
+  int64_t ss;
+  int32_t slots_i64;
+  int32_t vec_ok;  // 16-byte loads legal for both k and v
+  int32_t* status;
+};
+
+template <typename PoolT>
+struct Pack;
+template <>
+struct Pack<float> {
+  static constexpr int N = 4;
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+};
+template <>
+struct Pack<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+// Reads N consecutive d-elements of row (n, h) starting at d0 as floats.
+template <int N>
+__device__ __forceinline__ void read_run(const void* base, int64_t off, int64_t sd, int dtype,
+                                         bool vec, int64_t d0, int64_t D, float* f) {
+  if (vec && d0 + N <= D) {
+    if (dtype == B200_DTYPE_F32) {
+#pragma unroll
+      for (int i = 0; i < N; i += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + off + i);
+        f[i] = x.x;
+        f[i + 1] = x.y;
+        f[i + 2] = x.z;
+        f[i + 3] = x.w;
+      }
+      return;
+    }
+    if (dtype == B200_DTYPE_BF16) {
+#pragma unroll
+      for (int i = 0; i < N; i += 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(base) + off + i);
+        Elem<__nv_bfloat16>::unpack(raw, f + i);
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    f[i] = (d0 + i < D) ? load_elem(base, off + i * sd, dtype) : 0.f;
+}
+
+// One thread per (token, head, 16-byte chunk of the pool row).
+template <typename PoolT>
+__global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) {
+  constexpr int NE = Pack<PoolT>::N;
+  const int64_t chunks_per_head = (p.D + NE - 1) / NE;
+  const int64_t total = p.N * p.H * chunks_per_head;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = i % chunks_per_head;
+    const int64_t nh = i / chunks_per_head;
+    const int64_t h = nh % p.H;
+    const int64_t n = nh / p.H;
+    const int64_t slot = load_index(p.slots, n * p.ss, p.slots_i64);
+    if (slot < 0 || slot >= p.P * p.S) {
+      if (h == 0 && c == 0) report(p.status, B200_DEV_BAD_SLOT);
+      continue;
+    }
+    const int64_t d0 = c * NE;
+    const int64_t dst = ((p.layer_row0 + slot) * p.H + h) * p.D + d0;
+    float fk[NE], fv[NE];
+    read_run<NE>(p.k, n * p.ks0 + h * p.ks1 + d0 * p.ks2, p.ks2, p.in_dtype, p.vec_ok, d0, p.D, fk);
+    read_run<NE>(p.v, n * p.vs0 + h * p.vs1 + d0 * p.vs2, p.vs2, p.in_dtype, p.vec_ok, d0, p.D, fv);
+    if (d0 + NE <= p.D && ((p.D % NE) == 0)) {
+      *reinterpret_cast<uint4*>(static_cast<PoolT*>(p.kp) + dst) = Pack<PoolT>::pack(fk);
+      *reinterpret_cast<uint4*>(static_cast<PoolT*>(p.vp) + dst) = Pack<PoolT>::pack(fv);
+    } else {
+      for (int e = 0; e < NE && d0 + e < p.D; ++e) {
+        store_elem(p.kp, dst + e, p.pool_dtype, fk[e]);
+        store_elem(p.vp, dst + e, p.pool_dtype, fv[e]);
+      }
+    }
+  }
+}
+
+int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream) {
+  if (a.num_tokens == 0) return B200_OK;
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != B200_OK) return rc;
+  ScatterParams p{};
+  p.N = a.num_tokens;
+  p.H = a.pool.num_heads;
+  p.D = a.pool.head_dim;
+  p.S = a.pool.block_size;
+  p.P = a.pool.num_blocks;
+  p.layer_row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
+  p.k = a.k;
+  p.v = a.v;
+  p.ks0 = a.k_stride[0];
+  p.ks1 = a.k_stride[1];
+  p.ks2 = a.k_stride[2];
+  p.vs0 = a.v_stride[0];
+  p.vs1 = a.v_stride[1];
+  p.vs2 = a.v_stride[2];
+  p.in_dtype = a.kv_in_dtype;
+  p.kp = a.pool.k;
+  p.vp = a.pool.v;
+  p.pool_dtype = a.pool.dtype;
+  p.slots = a.slot_mapping;
+  p.ss = a.slot_stride;
+  p.slots_i64 = a.slot_dtype == B200_INDEX_I64;
+  p.status = a.status;
+  // Vector loads need unit innermost stride, 16-byte aligned rows and a
+  // 16-byte multiple for the head stride and token stride.
+  const size_t es = dtype_size(a.kv_in_dtype);
+  const int ne = a.pool.dtype == B200_DTYPE_F32 ? 4 : 8;
+  auto aligned = [&](const void* ptr, const int64_t* st) {
+    return st[2] == 1 && (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 &&
+           ((st[0] * es) % 16) == 0 && ((st[1] * es) % 16) == 0 && (ne * es) % 16 == 0;
+  };
+  p.vec_ok = (a.kv_in_dtype != B200_DTYPE_F16) && aligned(a.k, a.k_stride) && aligned(a.v, a.v_stride);
+  const int64_t total = p.N * p.H * ((p.D + ne - 1) / ne);
+  int64_t blocks = (total + 255) / 256;
+  blocks = std::min<int64_t>(blocks, static_cast<int64_t>(dev.num_sms) * 16);
+  if (a.pool.dtype == B200_DTYPE_F32)
+    kv_scatter_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  else
+    kv_scatter_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kv_scatter launch");
+  return B200_OK;
+}
+
+}  // namespace b200

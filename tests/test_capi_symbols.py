@@ -1,0 +1,83 @@
+"""The C-ABI library loads and exports every function the header declares.
+
+CPU-only: no entry point that launches device work is called here.
+"""
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "b200_paged_attn.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b200_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_expected_api():
+    names = declared_functions()
+    for fn in ("b200_kv_scatter", "b200_paged_decode", "b200_chunked_prefill",
+               "b200_chunked_prefill_batch", "b200_last_error"):
+        assert fn in names
+
+
+def test_library_exports_every_declared_symbol():
+    from b200attn import _lib
+
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} missing from {_lib.LIB_PATH}"
+    assert set(declared_functions()) <= set(_lib.SIGNATURES)
+    assert lib.b200_abi_version() == 1
+    assert lib.b200_built_arch() == 100
+
+
+def test_ctypes_struct_sizes_match_c_layout():
+    import ctypes
+    from b200attn import _lib
+
+    # Sizes computed from the C declarations on LP64 (8-byte pointers/int64,
+    # 4-byte enums padded to 8 where the next field is 8-aligned).
+    assert ctypes.sizeof(_lib.KVPool) == 64
+    assert ctypes.sizeof(_lib.ScatterArgs) == 64 + 8 * 4 + 48 + 8 + 8 + 8 + 8 + 8
+    assert ctypes.sizeof(_lib.PrefillBatchArgs) == 16
+
+
+def test_last_error_and_invalid_arguments_without_gpu():
+    import ctypes
+    from b200attn import _lib
+
+    lib = _lib.load()
+    # A null argument struct is rejected on the host before any CUDA call.
+    assert lib.b200_paged_decode(None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert "null" in _lib.last_error(lib)
+    args = _lib.DecodeArgs()  # all-zero pool: rejected as invalid, nothing launched
+    assert lib.b200_paged_decode(ctypes.byref(args), None) == _lib.ERR_INVALID_ARGUMENT
+    assert "KV pool" in _lib.last_error(lib)
+    sargs = _lib.ScatterArgs()
+    assert lib.b200_kv_scatter(ctypes.byref(sargs), None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_workspace_size_queries():
+    from b200attn import _lib
+
+    lib = _lib.load()
+    small = lib.b200_paged_decode_workspace_size(1, 8, 32, 1, 16, _lib.DTYPE_F32, 0)
+    assert small == 0  # one tile -> no split, no workspace
+    big = lib.b200_paged_decode_workspace_size(2, 32, 128, 2048, 16, _lib.DTYPE_BF16, 0)
+    assert big > 0
+
+
+def test_ops_reject_cpu_tensors_loudly():
+    from b200attn import paged_attention_batch_b200
+    import cases
+
+    c = cases.cfg1_case()
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_attention_batch_b200(c.q, c.pool, c.block_tables, c.context_lengths, 0)

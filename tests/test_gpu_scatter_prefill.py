@@ -1,0 +1,145 @@
+"""KV scatter and chunked-prefill parity on the GPU, through the C ABI.
+
+The scatter is integer/byte work: the pool after it must be bit-identical to
+the reference's write loop (pool digests in tests/golden/prefill_golden.json).
+The fp32 prefill must match the reference's SDPA v1/v2 and per-token outputs
+(max abs error <= 1e-4); bf16 prefill matches the fp32 oracle on the upcast
+inputs within 2e-2.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+PRE_META = json.loads((GOLDEN / "prefill_golden.json").read_text())
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def _case(name):
+    m = PRE_META[name]
+    return cases.prefill_case(m["prefix_len"], m["T"], m["H"], m["D"], m["S"], m["seed"])
+
+
+@pytest.mark.parametrize("name", sorted(PRE_META))
+def test_scatter_and_prefill_match_reference(name):
+    from b200attn import chunked_prefill_b200, kv_scatter_b200
+
+    golden = np.load(GOLDEN / "prefill_golden.npz")
+    c = _case(name)
+    d = _dev()
+    pool = c.pool.to(d)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    with torch.inference_mode():
+        kv_scatter_b200(c.k.to(d), c.v.to(d), pool, c.slots, c.layer_idx, status=status)
+        out = chunked_prefill_b200(c.q.to(d), pool, c.block_table, c.prefix_len, c.layer_idx,
+                                   status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert cases.digest(pool.k.cpu(), pool.v.cpu()) == PRE_META[name]["pool_after_digest"]
+    got = out.cpu()
+    for key in ("sdpa", "reference"):
+        want = torch.from_numpy(golden[f"{name}/{key}"])
+        err = (got - want).abs().max().item()
+        assert err <= 1e-4, f"{name} vs reference {key}: {err:.3e}"
+
+
+def test_scatter_strided_inputs_and_bf16_rounding():
+    from b200attn import kv_scatter_b200
+
+    d = _dev()
+    g = torch.Generator().manual_seed(3)
+    L, P, S, H, D, N = 2, 9, 16, 8, 32, 37
+    kp = torch.full((L, P, S, H, D), float("nan"), dtype=torch.bfloat16)
+    vp = kp.clone()
+    qkv = torch.randn((N, 3 * H * D), generator=g)  # k/v as strided views of a fused QKV
+    k = qkv[:, H * D:2 * H * D].view(N, H, D)
+    v = qkv[:, 2 * H * D:].view(N, H, D)
+    slots = torch.randperm(P * S, generator=g)[:N]
+    want_k, want_v = kp.clone(), vp.clone()
+    oracle.kv_scatter(want_k, want_v, k.to(torch.bfloat16), v.to(torch.bfloat16), slots, 1)
+    pool = cases.Pool(kp.to(d), vp.to(d), S)
+    kv_scatter_b200(k.to(d), v.to(d), pool, slots.to(d), 1)
+    torch.cuda.synchronize()
+    assert cases.digest(pool.k.cpu(), pool.v.cpu()) == cases.digest(want_k, want_v)
+    # Non-unit innermost stride takes the element path.
+    kt = torch.randn((N, D, H), generator=g).transpose(1, 2)
+    pool32 = cases.Pool(torch.zeros((1, P, S, H, D), device=d), torch.zeros((1, P, S, H, D), device=d), S)
+    kv_scatter_b200(kt.to(d), kt.to(d), pool32, slots.tolist(), 0)
+    want32 = torch.zeros((1, P, S, H, D))
+    oracle.kv_scatter(want32, want32.clone(), kt, kt, slots, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(pool32.k.cpu(), want32)
+
+
+def test_scatter_bad_slot_is_flagged_not_written():
+    from b200attn import _lib, kv_scatter_b200
+
+    d = _dev()
+    pool = cases.Pool(torch.zeros((1, 4, 4, 2, 8), device=d), torch.zeros((1, 4, 4, 2, 8), device=d), 4)
+    k = torch.ones((2, 2, 8), device=d)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    kv_scatter_b200(k, k, pool, [3, 4 * 4 + 2], 0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & _lib.DEV_BAD_SLOT
+    assert float(pool.k.sum()) == 16.0  # only the valid slot was written
+
+
+@pytest.mark.parametrize("prefix,T,seed", [(0, 64, 1), (16, 64, 2), (37, 5, 3), (1000, 64, 4),
+                                           (256, 200, 5), (4032, 64, 6), (96, 512, 7)])
+def test_prefill_bf16_kv_against_oracle(prefix, T, seed):
+    from b200attn import chunked_prefill_b200, kv_scatter_b200
+
+    c = cases.prefill_case(prefix, T, 32, 128, 16, seed, dtype=torch.bfloat16, n_layer=1,
+                           layer_idx=0)
+    d = _dev()
+    pool = c.pool.to(d)
+    kv_scatter_b200(c.k.to(d), c.v.to(d), pool, c.slots, 0)
+    out = chunked_prefill_b200(c.q.to(d), pool, c.block_table, prefix, 0)
+    torch.cuda.synchronize()
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    oracle.kv_scatter(kp, vp, c.k, c.v, c.slots, 0)
+    want = oracle.prefix_prefill_from_pool(c.q.float(), kp.float(), vp.float(), c.block_table,
+                                           prefix, 0, compute_dtype=torch.float64).float()
+    err = (out.float().cpu() - want).abs().max().item()
+    assert err <= 2e-2, f"max abs {err:.3e}"
+
+
+def test_prefill_batch_matches_single_calls():
+    from b200attn import chunked_prefill_b200, chunked_prefill_batch_b200, kv_scatter_b200
+
+    d = _dev()
+    specs = [(0, 64, 11), (48, 64, 12), (500, 17, 13)]
+    cs = [cases.prefill_case(p, t, 32, 128, 16, s, dtype=torch.bfloat16, n_layer=1,
+                             layer_idx=0) for p, t, s in specs]
+    # One shared pool: give each sequence its own block range.
+    S, H, D = 16, 32, 128
+    sizes = [c.pool.k.shape[1] for c in cs]
+    kp = torch.cat([c.pool.k for c in cs], dim=1).to(d)
+    vp = torch.cat([c.pool.v for c in cs], dim=1).to(d)
+    pool = cases.Pool(kp, vp, S)
+    tables, qs, offs = [], [], 0
+    for c, n in zip(cs, sizes):
+        table = [x + offs for x in c.block_table]
+        slots = [s + offs * S for s in c.slots]
+        kv_scatter_b200(c.k.to(d), c.v.to(d), pool, slots, 0)
+        tables.append(table)
+        qs.append(c.q.to(d))
+        offs += n
+    outs = chunked_prefill_batch_b200(qs, pool, tables, [c.prefix_len for c in cs], 0)
+    for q, t, c, o in zip(qs, tables, cs, outs):
+        single = chunked_prefill_b200(q, pool, t, c.prefix_len, 0)
+        torch.cuda.synchronize()
+        assert torch.equal(single.cpu(), o.cpu())
