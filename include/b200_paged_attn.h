@@ -126,8 +126,8 @@ typedef struct {
  * Split-K: long contexts are cut into splits processed by different CTAs;
  * partial results go to `workspace` and the last CTA of a (sequence, head
  * group) combines them.  `workspace` must hold
- * b200_paged_decode_workspace_size(...) bytes; its counter area must be
- * zero before the first call (the kernels leave it zero afterwards).
+ * b200_paged_decode_workspace_size(...) bytes; its contents need not be
+ * initialised (the launch clears the split counters on `stream` first).
  *
  * Virtual-batch mode (used by the fp32 chunked prefill): when
  * context_lengths is NULL, context_lengths[b] = ctx_base + b + 1 and

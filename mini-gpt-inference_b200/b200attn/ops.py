@@ -69,8 +69,8 @@ def _strides3(t: torch.Tensor):
 class _Workspace:
     """Per (device, stream) split-K scratch, grown on demand.
 
-    The counter area must start at zero; the kernels leave it zero after
-    every call, so the buffer is zeroed only when it is (re)allocated.
+    Its contents need not be initialised: every decode launch clears its
+    split counters on the stream first.
     """
 
     def __init__(self):

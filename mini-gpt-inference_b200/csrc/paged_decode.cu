@@ -603,6 +603,11 @@ int launch_paged_decode(const DecodeLaunch& a, cudaStream_t stream) {
     prm.ws_ml = reinterpret_cast<float*>(ws + acc_bytes);
     size_t cnt_off = (acc_bytes + ml_bytes + 255) & ~size_t(255);
     prm.ws_cnt = reinterpret_cast<int32_t*>(ws + cnt_off);
+    // The counters' location depends on (B, H, splits), so a workspace
+    // reused across calls of other shapes may hold stale data there; clear
+    // them on the stream before the launch (an async memset, no allocation).
+    cudaError_t me = cudaMemsetAsync(prm.ws_cnt, 0, static_cast<size_t>(a.batch * num_hg) * sizeof(int32_t), stream);
+    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(split-K counters)");
   }
 
   // Tensor maps over the [L*P*S rows, H, D] views of the pools.

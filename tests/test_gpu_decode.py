@@ -58,10 +58,29 @@ def test_decode_matches_reference_golden(case, splits):
     assert int(status.item()) == 0
     got = out.cpu()
     assert torch.isfinite(got).all()
+    # The scale-8 large-logit case uses the reference's own tolerance for it
+    # (tests/test_triton_paged_decode.py:66-71, atol 5e-4): outputs reach ~21
+    # and the reference's two fp32 paths already differ by 1.3e-4 there.
+    tol = 5e-4 if "_sc8.0_" in case.name else FP32_ATOL
     for key in ("online", "dense"):
         want = torch.from_numpy(golden[f"{case.name}/{key}"])
         err = (got - want).abs().max().item()
-        assert err <= FP32_ATOL, f"{case.name} vs reference {key}: max abs {err:.3e}"
+        assert err <= tol, f"{case.name} vs reference {key}: max abs {err:.3e}"
+
+
+def test_workspace_reuse_across_shapes():
+    # A split-K call of one shape leaves partials where a call of another
+    # shape keeps its counters; the second call must still be exact.
+    big = cases.bf16_case(40, 32, 128, 16, 3000, 21)
+    small = cases.ragged_case(batch=4, length=129, heads=8, dim=32, seed=20261163)
+    for _ in range(2):
+        for case, tol in ((big, BF16_ATOL), (small, FP32_ATOL)):
+            q, pool, tables, lens = _on(case)
+            out = _decode(q, pool, tables, lens, case.layer_idx)
+            want = oracle.paged_decode_dense(case.q, case.pool.k.float(), case.pool.v.float(),
+                                             case.block_tables, case.context_lengths,
+                                             case.layer_idx, compute_dtype=torch.float64).float()
+            assert (out.cpu() - want).abs().max().item() <= tol
 
 
 @pytest.mark.parametrize("case", [cases.cfg1_case(),
