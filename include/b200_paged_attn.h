@@ -213,6 +213,22 @@ B200_API int b200_paged_decode(const b200_decode_args_t* args, void* stream);
 B200_API int b200_chunked_prefill(const b200_prefill_args_t* args, void* stream);
 B200_API int b200_chunked_prefill_batch(const b200_prefill_batch_args_t* args, void* stream);
 
+/*
+ * Paged decode that allocates nothing -- no counterpart in the reference.
+ * For callers that may not allocate device memory (an engine that owns all
+ * memory up front, a plugin restricted to the buffers it is given, a step
+ * loop that must not call cudaMalloc): same arguments and results as
+ * b200_paged_decode, but args->workspace / workspace_bytes are ignored and
+ * the split-K scratch is a static device array of
+ * B200_NO_ALLOC_SCRATCH_BYTES held by every GPU that loads the library.
+ * Calls needing more scratch are rejected with B200_ERR_UNSUPPORTED.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the
+ * GPU race and must be serialised by the caller.
+ */
+#define B200_NO_ALLOC_SCRATCH_BYTES (4u << 20)
+B200_API int b200_paged_decode_no_alloc(const b200_decode_args_t* args, void* stream);
+
 /* Workspace bytes the decode launch needs for these sizes. */
 B200_API size_t b200_paged_decode_workspace_size(int64_t batch, int64_t num_heads,
                                         int64_t head_dim, int64_t table_width,

@@ -28,6 +28,9 @@ DEV_BAD_SLOT = 4
 DEV_WAIT_TIMEOUT = 8
 DEV_SLOT_MISMATCH = 16
 
+# Static split-K scratch of b200_paged_decode_no_alloc (B200_NO_ALLOC_SCRATCH_BYTES).
+NO_ALLOC_SCRATCH_BYTES = 4 << 20
+
 _i64 = ctypes.c_int64
 _p = ctypes.c_void_p
 
@@ -79,6 +82,7 @@ SIGNATURES = {
     "b200_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _p]),
     "b200_chunked_prefill": (ctypes.c_int, [ctypes.POINTER(PrefillArgs), _p]),
     "b200_chunked_prefill_batch": (ctypes.c_int, [ctypes.POINTER(PrefillBatchArgs), _p]),
+    "b200_paged_decode_no_alloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _p]),
     "b200_paged_decode_workspace_size": (
         ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int32]),
     "b200_chunked_prefill_workspace_size": (

@@ -22,7 +22,8 @@ OUT_DIR = PKG_ROOT / "b200attn"
 LIB_NAME = "libb200attn.so"
 BUILD_DIR = PKG_ROOT / "_build"
 
-SOURCES = ["host_util.cu", "capi.cu", "kv_scatter.cu", "paged_decode.cu", "prefill_tc.cu"]
+SOURCES = ["host_util.cu", "capi.cu", "kv_scatter.cu", "paged_decode.cu", "paged_decode_no_alloc.cu",
+           "prefill_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
