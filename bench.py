@@ -56,24 +56,25 @@ def measured_peak() -> tuple[float, str]:
 
 # ------------------------------------------------------------------ workload
 class Workload:
-    def __init__(self, name: str, rank: int, world: int, device: torch.device):
+    def __init__(self, name: str, rank: int, world: int, device: torch.device,
+                 batch: int | None = None, ctx: int | None = None):
         self.name = name
         self.H, self.D, self.S = 32, 128, 16
         self.kv_dtype = torch.bfloat16
         self.q_dtype = torch.bfloat16
         if name == "cfg4":
-            self.B = 64
-            lens = [32768] * self.B
-            self.desc = ("config 4: long-context split-K decode, bf16 KV, 64 requests/GPU "
-                         "x 32768 tokens, H=32, D=128, S=16, fused KV write")
+            self.B = batch or 64
+            lens = [ctx or 32768] * self.B
+            self.desc = (f"config 4: long-context split-K decode, bf16 KV, {self.B} requests/GPU "
+                         f"x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
         elif name == "cfg3":
-            self.B = 256
+            self.B = batch or 256
             g = torch.Generator().manual_seed(1000 + rank)
             lens = torch.randint(1, 4097, (self.B,), generator=g).tolist()
             lens[0] = 1
             if lens[-1] % self.S == 0:
                 lens[-1] -= 1
-            self.desc = ("config 3: ragged decode, bf16 KV, batch 256/GPU, contexts "
+            self.desc = (f"config 3: ragged decode, bf16 KV, batch {self.B}/GPU, contexts "
                          "~U[1,4096], H=32, D=128, S=16, fused KV write")
         else:
             raise SystemExit(f"unknown workload {name}")
@@ -271,7 +272,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if pg:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    wl = Workload(args.workload, rank, world, dev)
+    wl = Workload(args.workload, rank, world, dev, args.batch, args.ctx)
     stream = torch.cuda.current_stream(dev)
 
     def step(q, k_new, v_new, tables, ctx, slots, out):
@@ -340,7 +341,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": wl.desc, "batch_per_gpu": wl.B, "global_batch": wl.B * world,
-                       "context_lens": "32768" if args.workload == "cfg4" else "U[1,4096]",
+                       "context_lens": str(wl.lens[0]) if args.workload == "cfg4" else "U[1,4096]",
                        "heads": wl.H, "head_dim": wl.D, "block_size": wl.S,
                        "kv_dtype": "bf16", "q_dtype": "bf16", "accumulate": "f32",
                        "fused_kv_write": True,
@@ -373,6 +374,10 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("cfg4", "cfg3"), default="cfg4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="requests per GPU (default: the workload's; smaller for profiling)")
+    ap.add_argument("--ctx", type=int, default=None,
+                    help="context length of cfg4 requests (default 32768)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
