@@ -154,4 +154,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
+// Packed fp32x2 fused multiply-add (one sm_100 instruction for two lanes of
+// work): returns a * b + c element-wise, each with a single rounding.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// Exact bf16 pair (one 32-bit word, element 0 in the low half) -> float2.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 }  // namespace b200
