@@ -11,6 +11,8 @@ KVCacheCausalSelfAttention.forward_prefill_chunk -- runs them on the
 deterministic inputs of tests/golden/cases.py and writes
   decode_golden.npz / decode_golden.json    (decode outputs + input digests)
   prefill_golden.npz / prefill_golden.json  (prefill outputs, pool digests)
+  e2e_golden.json                           (MiniRuntime greedy tokens and counts,
+                                             configuration 2, ample and capped KV)
 It also checks that cases.py reproduces the reference's input builders
 bit for bit.  The GPU box never runs this script; it only reads the files.
 """
@@ -173,6 +175,90 @@ def prefill_fixtures(ref) -> tuple[dict, dict]:
     return arrays, meta
 
 
+CFG2 = {"n_embd": 256, "n_head": 8, "n_layer": 4, "vocab": 256, "pos": 296,
+        "prompts": [128, 256, 128, 256], "output_len": 8, "block_size": 16,
+        "token_budget": 64, "max_running": 4,
+        "runs": {"ample": {"num_blocks": 52, "policy": "conservative"},
+                 "capped": {"num_blocks": 26, "policy": "recompute"}}}
+
+
+def cfg2_prompts() -> list[list[int]]:
+    """Configuration 2 prompts: randint(0, 256) with one seed-0 generator."""
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, CFG2["vocab"], (p,), generator=g).tolist() for p in CFG2["prompts"]]
+
+
+def e2e_fixtures(ref) -> dict:
+    """Runs the reference MiniRuntime on configuration 2 (fp32, CPU)."""
+    sys.path.insert(0, str(HERE.parents[1] / "mini-gpt-inference_b200"))
+    from b200attn.harness.model import init_weights
+    from minivllm.block_manager import BlockManager
+    from minivllm.kv_block_pool import KVBlockPool
+    from minivllm.mini_runtime import MiniRuntime
+    from minivllm.model import MiniGPT
+    from minivllm.model_runner import ModelRunner
+    from minivllm.scheduler import Scheduler
+    from minivllm.sequence import SequenceState, Status
+
+    model = MiniGPT(n_embd=CFG2["n_embd"], n_head=CFG2["n_head"], vocab_size=CFG2["vocab"],
+                    block_size=CFG2["pos"], dropout=0.0, n_layer=CFG2["n_layer"]).eval()
+    init_weights(model, seed=0)
+    prompts = cfg2_prompts()
+    out = {"config": CFG2, "prompt_digest": cases.digest(*[torch.tensor(p) for p in prompts])}
+    for run_name, run in CFG2["runs"].items():
+        for prefill_mode in ("sdpa_v2", "reference"):
+            model.set_prefill_fastpath_mode(prefill_mode)
+            model.set_decode_attention_backend("reference")
+            bm = BlockManager(run["num_blocks"], CFG2["block_size"])
+            pool = KVBlockPool(CFG2["n_layer"], run["num_blocks"], CFG2["block_size"],
+                               CFG2["n_head"], CFG2["n_embd"] // CFG2["n_head"])
+            rt = MiniRuntime.__new__(MiniRuntime)
+            rt.block_manager = bm
+            rt.scheduler = Scheduler(bm, max_running=CFG2["max_running"],
+                                     max_num_batched_tokens=CFG2["token_budget"],
+                                     preemption_policy=run["policy"])
+            rt.runner = ModelRunner(model, pool, bm)
+            rt.iteration = 0
+            rt.records = []
+            rt.sync_cuda_timing = False
+            rt.verbose = False
+            rt._kv_high_watermark = {}
+            margins = []
+            orig = rt.runner.decode_batch
+
+            def probe(seqs, _orig=orig):
+                logits, toks = _orig(seqs)
+                top = torch.topk(logits, 2, dim=-1).values
+                margins.extend((top[:, 0] - top[:, 1]).tolist())
+                return logits, toks
+
+            rt.runner.decode_batch = probe
+            reqs = [SequenceState(seq_id=f"r{i}", prompt_tokens=p,
+                                  max_tokens=len(p) + CFG2["output_len"])
+                    for i, p in enumerate(prompts)]
+            for r in reqs:
+                rt.add_request(r)
+            with torch.inference_mode():
+                for _ in range(1000):
+                    if all(r.status is Status.FINISHED for r in reqs):
+                        break
+                    rt.step()
+            bm.check_invariants(reqs)
+            summ = rt.metrics_summary()
+            key = f"{run_name}/{prefill_mode}"
+            out[key] = {
+                "tokens": {r.seq_id: list(r.generated_tokens) for r in reqs},
+                "counts": {k: summ[k] for k in ("iterations", "scheduled_tokens",
+                                                "prefill_tokens", "decode_tokens",
+                                                "output_tokens", "preemptions",
+                                                "repeated_kv_tokens")},
+                "min_decode_logit_margin": min(margins),
+            }
+            print(key, out[key]["counts"], "min margin", round(min(margins), 5))
+        assert out[f"{run_name}/sdpa_v2"]["tokens"] == out[f"{run_name}/reference"]["tokens"]
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -189,6 +275,8 @@ def main():
     arrays, meta = prefill_fixtures(args.reference)
     np.savez_compressed(out / "prefill_golden.npz", **arrays)
     (out / "prefill_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
+    e2e = e2e_fixtures(args.reference)
+    (out / "e2e_golden.json").write_text(json.dumps(e2e, indent=1, sort_keys=True))
     print("wrote fixtures to", out)
 
 

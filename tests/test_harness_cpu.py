@@ -1,0 +1,94 @@
+"""Runtime harness on the CPU: end-to-end parity with the reference runtime
+(configuration 2, golden tokens and counts from the reference MiniRuntime)
+and scheduler invariants under seeded random workloads."""
+from __future__ import annotations
+
+import random
+
+import pytest
+import torch
+
+from e2e_common import GOLDEN, run_cfg2
+from oracle_backend import OracleBackend
+
+
+@pytest.mark.parametrize("run_name", ["ample", "capped"])
+def test_cfg2_tokens_and_counts_match_reference(run_name):
+    torch.set_num_threads(4)
+    tokens, counts, _ = run_cfg2(run_name, "cpu", backend=OracleBackend())
+    want = GOLDEN[f"{run_name}/sdpa_v2"]
+    assert tokens == want["tokens"]
+    assert counts == want["counts"]
+    if run_name == "capped":
+        assert counts["preemptions"] > 0 and counts["repeated_kv_tokens"] > 0
+
+
+class FakeRunner:
+    """Stands in for ModelRunner: reserves KV like the real one, no model."""
+
+    def __init__(self, bm):
+        self.bm = bm
+        self.kv = {}
+
+    def prefill_chunk(self, seq, start_pos, num_tokens):
+        assert start_pos == seq.prompt_pos == seq.length
+        self.bm.reserve_slots(seq, num_tokens)
+        seq.length += num_tokens
+        return torch.zeros(1, num_tokens, 4)
+
+    def decode_batch(self, seqs):
+        for s in seqs:
+            self.bm.reserve_append_slot(s)
+            s.length += 1
+        toks = [(s.length * 7 + len(s.generated_tokens)) % 4 for s in seqs]
+        return torch.zeros(len(seqs), 4), toks
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_scheduler_invariants_random_workloads(seed):
+    from b200attn.harness import (BlockManager, MiniRuntime, Scheduler, SequenceState, Status)
+
+    rng = random.Random(seed)
+    bs = rng.choice([4, 8, 16])
+    policy = rng.choice(["conservative", "recompute"])
+    reqs = []
+    for i in range(rng.randint(1, 7)):
+        p = rng.randint(1, 40)
+        reqs.append(SequenceState(seq_id=f"q{i}", prompt_tokens=[1] * p,
+                                  max_tokens=p + rng.randint(1, 12)))
+    need = max(-(-(r.max_tokens - 1) // bs) for r in reqs)
+    nblocks = need + rng.randint(0, 6)
+    bm = BlockManager(nblocks, bs)
+    sch = Scheduler(bm, max_running=rng.randint(1, 4),
+                    max_num_batched_tokens=rng.randint(4, 48), preemption_policy=policy)
+    rt = MiniRuntime(FakeRunner(bm), sch)
+    for r in reqs:
+        rt.add_request(r)
+    for _ in range(2000):
+        if all(r.status is Status.FINISHED for r in reqs):
+            break
+        rt.step()
+        bm.check_invariants([r for r in reqs if r.status is not Status.WAITING])
+    else:
+        raise AssertionError("workload did not finish")
+    assert not bm.block_owner
+    for r in reqs:
+        assert len(r.generated_tokens) == r.max_tokens - r.prompt_length
+    s = rt.metrics_summary()
+    assert s["output_tokens"] == sum(len(r.generated_tokens) for r in reqs)
+    if policy == "conservative":
+        assert s["preemptions"] == 0
+
+
+def test_harness_rejects_requests_like_the_reference():
+    from b200attn.harness import BlockManager, Scheduler, SequenceState
+
+    sch = Scheduler(BlockManager(2, 4), max_running=1, max_num_batched_tokens=8)
+    with pytest.raises(ValueError):
+        sch.add_request(SequenceState(seq_id="a", prompt_tokens=[], max_tokens=3))
+    with pytest.raises(ValueError):
+        sch.add_request(SequenceState(seq_id="b", prompt_tokens=[1, 2], max_tokens=2))
+    with pytest.raises(ValueError):
+        sch.add_request(SequenceState(seq_id="c", prompt_tokens=[1] * 8, max_tokens=20))
+    with pytest.raises(ValueError):
+        Scheduler(BlockManager(2, 4), 1, 8, preemption_policy="lru")
