@@ -126,7 +126,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 3-D tiled TMA load (no multicast) into CTA shared memory, completing
+// 3-D tiled TMA load into this CTA's own shared memory, completing
 // `bytes` on the mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2) {

@@ -8,7 +8,7 @@
 // Warp roles (6 warps):
 //   warp 0   TMA producer: for each 128-key tile walks the block table and
 //            loads, per KV block, boxes {64 d, 1 head, rbox rows} of K and V
-//            with 128-byte swizzle (no multicast) into a 2-stage ring.
+//            with 128-byte swizzle into a 2-stage ring of this CTA.
 //   warp 1   TMEM allocation (256 columns) and the MMA issuer (one thread):
 //              S   = Q K^T   -> TMEM columns [0, 128)         (M=128,N=128)
 //              O  += P V     -> TMEM columns [128, 128+D)      (M=128,N=D)
