@@ -1,23 +1,30 @@
-"""Benchmark of the sm_100a paged decode attention (fused KV write + split-K).
+"""Benchmark of the sm_100a paged-attention backend.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg4|cfg3]
+                    [--workload cfg4|cfg3|cfg5-t512|cfg5-t64|scatter]
 
-One step = one launch of the fused KV-write + batched paged decode attention
-kernel over one batch (one layer) of the workload:
+One step = one launch of the hot path over one batch of the workload, with
+inputs resident in HBM (``value``), and the same step through the public
+Python API with the step's inputs copied from pinned host memory and its
+result copied back, plus a host synchronisation (``e2e``):
 
-* cfg4 (default): configuration 4 -- bf16 KV, 64 requests per GPU, every
-  context 32768 tokens, 32 heads x 128 dims, block size 16, randomly
-  permuted block tables; 34.4 GB of KV per GPU (larger than the 126 MB L2,
-  so no flush is needed between steps).  Requests are sharded across GPUs
-  (weak scaling: each rank owns 64 requests of the global 64*N batch).
+* cfg4 (default): configuration 4 -- fused KV write + paged decode, bf16 KV,
+  64 requests per GPU, every context 32768 tokens, 32 heads x 128 dims, block
+  size 16, randomly permuted block tables; 34.7 GB of KV per GPU (larger than
+  the 126 MB L2, so no flush is needed between steps).  Requests are sharded
+  across GPUs (weak scaling: each rank owns 64 requests of the global batch).
 * cfg3: configuration 3 at batch 256 -- ragged contexts ~U[1, 4096].
+* cfg5-t512 / cfg5-t64: configuration 5 -- one batched tcgen05 chunked
+  prefill launch over 16 sequences, chunk 512 or 64 tokens, prefixes
+  16*U{0..252}; the KV pool is ~2-4 GB (larger than L2).
+* scatter: the slot-mapping KV scatter of 16 x 512 prefill tokens (bf16).
 
 Under torchrun (N>1) each rank runs its shard on its own GPU; the only
-collective is the all-reduce(MAX) of the timing.  Rank 0 prints one JSON
+collective is the all-reduce(MAX) of the timings.  Rank 0 prints one JSON
 line.  ``--impl reference`` times the reference algorithm's CPU restatement
-(oracle/, paged_attention_batch_online_v1 of minivllm) on the host cores
-instead; under torchrun only rank 0 runs it.
+(oracle/: paged_attention_batch_online_v1, the SDPA v2 prefill, the KV
+write loop of minivllm) on the host cores instead; under torchrun only
+rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -30,15 +37,17 @@ import subprocess
 import sys
 import time
 from pathlib import Path
+from types import SimpleNamespace
 
 import torch
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "mini-gpt-inference_b200"))
 
-METRIC = ("paged decode attn HBM GB/s (% of 8 TB/s); decode tokens/sec at 1/2/4/8 B200")
+METRIC = "paged decode attn HBM GB/s (% of 8 TB/s); decode tokens/sec at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
-FALLBACK_HBM_GBS = 6650.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+H, D, S = 32, 128, 16
 
 
 def env_rank():
@@ -46,88 +55,245 @@ def env_rank():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-def measured_peak() -> tuple[float, str]:
-    p = REPO / "MEASURED_PEAKS.json"
+def measured_peak(key: str) -> tuple[float, str]:
     try:
-        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        return float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())[key]), "measured"
     except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
+        return FALLBACK[key], "fallback"
 
 
-# ------------------------------------------------------------------ workload
-class Workload:
-    def __init__(self, name: str, rank: int, world: int, device: torch.device,
-                 batch: int | None = None, ctx: int | None = None):
-        self.name = name
-        self.H, self.D, self.S = 32, 128, 16
-        self.kv_dtype = torch.bfloat16
-        self.q_dtype = torch.bfloat16
+def _tables(counts, perm):
+    width = max(counts)
+    t = torch.full((len(counts), width), -1, dtype=torch.int64)
+    nxt = 0
+    for b, c in enumerate(counts):
+        t[b, :c] = perm[nxt:nxt + c]
+        nxt += c
+    return t
+
+
+# ------------------------------------------------------------------ workloads
+class DecodeWorkload:
+    """Fused KV write + paged decode over one batch (configuration 4 or 3)."""
+
+    bound, unit = "hbm", "GB/s"
+
+    def __init__(self, name, rank, device, batch=None, ctx=None):
+        self.name, self.device = name, device
         if name == "cfg4":
             self.B = batch or 64
             lens = [ctx or 32768] * self.B
-            self.desc = (f"config 4: long-context split-K decode, bf16 KV, {self.B} requests/GPU "
-                         f"x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
-        elif name == "cfg3":
+            self.desc = (f"config 4: long-context split-K decode, bf16 KV, {self.B} requests/GPU"
+                         f" x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
+        else:
             self.B = batch or 256
             g = torch.Generator().manual_seed(1000 + rank)
             lens = torch.randint(1, 4097, (self.B,), generator=g).tolist()
             lens[0] = 1
-            if lens[-1] % self.S == 0:
+            if lens[-1] % S == 0:
                 lens[-1] -= 1
-            self.desc = (f"config 3: ragged decode, bf16 KV, batch {self.B}/GPU, contexts "
-                         "~U[1,4096], H=32, D=128, S=16, fused KV write")
-        else:
-            raise SystemExit(f"unknown workload {name}")
+            self.desc = (f"config 3: ragged decode, bf16 KV, batch {self.B}/GPU, contexts"
+                         " ~U[1,4096], H=32, D=128, S=16, fused KV write")
         self.lens = lens
-        counts = [math.ceil(n / self.S) for n in lens]
-        self.counts = counts
+        counts = [math.ceil(n / S) for n in lens]
         P = sum(counts) + max(1, sum(counts) // 100)
-        self.P = P
         g = torch.Generator(device=device).manual_seed(20260000 + rank)
-        shape = (1, P, self.S, self.H, self.D)
-        self.k = torch.empty(shape, dtype=self.kv_dtype, device=device)
-        self.v = torch.empty(shape, dtype=self.kv_dtype, device=device)
-        self.k.normal_(generator=g)
-        self.v.normal_(generator=g)
-        perm = torch.randperm(P, generator=g, device=device).cpu()
-        M = max(counts)
-        tables = torch.full((self.B, M), -1, dtype=torch.int64)
-        nxt = 0
-        for b, c in enumerate(counts):
-            tables[b, :c] = perm[nxt:nxt + c]
-            nxt += c
-        self.tables_h = tables.pin_memory()
-        self.lens_h = torch.tensor(lens, dtype=torch.int64).pin_memory()
-        slots = [int(tables[b, (n - 1) // self.S]) * self.S + (n - 1) % self.S
-                 for b, n in enumerate(lens)]
-        self.slots_h = torch.tensor(slots, dtype=torch.int64).pin_memory()
-        self.q_h = torch.randn((self.B, self.H, self.D), generator=torch.Generator().manual_seed(rank)
-                               ).to(self.q_dtype).pin_memory()
-        self.knew_h = torch.randn((self.B, self.H, self.D), generator=torch.Generator().manual_seed(rank + 1)
-                                  ).to(self.kv_dtype).pin_memory()
-        self.vnew_h = torch.randn((self.B, self.H, self.D), generator=torch.Generator().manual_seed(rank + 2)
-                                  ).to(self.kv_dtype).pin_memory()
-        self.tables = self.tables_h.to(device)
-        self.ctx = self.lens_h.to(device)
-        self.slots = self.slots_h.to(device)
-        self.q = self.q_h.to(device)
-        self.k_new = self.knew_h.to(device)
-        self.v_new = self.vnew_h.to(device)
-        self.out_h = torch.empty((self.B, self.H, self.D), dtype=self.q_dtype).pin_memory()
+        self.k = torch.empty((1, P, S, H, D), dtype=torch.bfloat16, device=device).normal_(generator=g)
+        self.v = torch.empty_like(self.k).normal_(generator=g)
+        tables = _tables(counts, torch.randperm(P, generator=g, device=device).cpu())
+        slots = [int(tables[b, (n - 1) // S]) * S + (n - 1) % S for b, n in enumerate(lens)]
+        hg = torch.Generator().manual_seed(rank)
+        self.host = {
+            "q": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
+            "k_new": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
+            "v_new": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
+            "tables": tables.pin_memory(),
+            "ctx": torch.tensor(lens, dtype=torch.int64).pin_memory(),
+            "slots": torch.tensor(slots, dtype=torch.int64).pin_memory(),
+        }
+        self.dev = {k: v.to(device) for k, v in self.host.items()}
+        self.out_h = torch.empty((self.B, H, D), dtype=torch.bfloat16).pin_memory()
+        self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
+        self.kv_gb = 2 * self.k.numel() * self.k.element_size() / 1e9
 
-    @property
-    def pool(self):
-        from types import SimpleNamespace
-        return SimpleNamespace(k=self.k, v=self.v, block_size=self.S)
+    def _call(self, t, prepare=False, out=None):
+        from b200attn import paged_attention_batch_b200
+        return paged_attention_batch_b200(t["q"], self.pool, t["tables"], t["ctx"], 0,
+                                          k_new=t["k_new"], v_new=t["v_new"],
+                                          slot_mapping=t["slots"], out=out, prepare=prepare)
 
-    def bytes_per_step(self) -> int:
+    def prepare(self):
+        self.call = self._call(self.dev, prepare=True,
+                               out=torch.empty((self.B, H, D), dtype=torch.bfloat16,
+                                               device=self.device))
+
+    def step(self):
+        self.call()
+
+    def e2e_step(self):
+        t = {k: v.to(self.device, non_blocking=True) for k, v in self.host.items()}
+        self.out_h.copy_(self._call(t), non_blocking=True)
+
+    def work(self) -> float:  # algorithmic bytes per step
         from b200attn import decode_bytes
-        return decode_bytes(self.lens, self.H, self.D, self.S, kv_bytes=2, q_bytes=2,
-                            out_bytes=2, idx_bytes=8, fused_in_bytes=2)
+        return decode_bytes(self.lens, H, D, S, kv_bytes=2, q_bytes=2, out_bytes=2, idx_bytes=8,
+                            fused_in_bytes=2)
 
-    def h2d_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in
-                   (self.q_h, self.knew_h, self.vnew_h, self.tables_h, self.lens_h, self.slots_h))
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in self.host.values())
+
+    def d2h_bytes(self):
+        return self.out_h.numel() * self.out_h.element_size()
+
+    def config(self, world):
+        return {"workload": self.desc, "batch_per_gpu": self.B, "global_batch": self.B * world,
+                "context_lens": str(self.lens[0]) if self.name == "cfg4" else "U[1,4096]",
+                "heads": H, "head_dim": D, "block_size": S, "kv_dtype": "bf16",
+                "q_dtype": "bf16", "accumulate": "f32", "fused_kv_write": True,
+                "l2": "inputs larger than L2 (KV pool %.1f GB per GPU), no flush" % self.kv_gb,
+                "parallelism": f"request-sharded dp{world} (no data-path collective)"}
+
+    def extra(self, ms_max, world, steps):
+        value = self.work() * world * steps / (ms_max * 1e-3) / 1e9
+        return {"pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
+                "decode_tokens_per_s": self.B * world * steps / (ms_max * 1e-3)}
+
+
+class PrefillWorkload:
+    """One batched tcgen05 chunked-prefill launch over 16 sequences (configuration 5)."""
+
+    unit = "TFLOP/s"
+
+    def __init__(self, T, rank, device, nseq=16):
+        self.T, self.device, self.nseq = T, device, nseq
+        self.bound = "tensor" if T >= 512 else "hbm"
+        g = torch.Generator().manual_seed(rank)
+        self.prefix = (torch.randint(0, 253, (nseq,), generator=g) * 16).tolist()
+        counts = [math.ceil((p + T) / S) for p in self.prefix]
+        P = sum(counts) + 16
+        gd = torch.Generator(device=device).manual_seed(30260000 + rank)
+        self.k = torch.empty((1, P, S, H, D), dtype=torch.bfloat16, device=device).normal_(generator=gd)
+        self.v = torch.empty_like(self.k).normal_(generator=gd)
+        perm = torch.randperm(P, generator=gd, device=device).cpu()
+        self.tables_h, nxt = [], 0
+        for c in counts:
+            self.tables_h.append(perm[nxt:nxt + c].clone().pin_memory())
+            nxt += c
+        self.q_h = [torch.randn((T, H, D), generator=g).to(torch.bfloat16).pin_memory()
+                    for _ in range(nseq)]
+        self.tables = [t.to(device) for t in self.tables_h]
+        self.q = [q.to(device) for q in self.q_h]
+        self.out_h = [torch.empty((T, H, D), dtype=torch.bfloat16).pin_memory() for _ in range(nseq)]
+        self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
+        self.kv_gb = 2 * self.k.numel() * self.k.element_size() / 1e9
+        self.desc = (f"config 5: prefix-aware chunked prefill (tcgen05), bf16, {nseq} sequences,"
+                     f" chunk {T}, prefixes 16*U{{0..252}}, H=32, D=128, S=16")
+
+    def prepare(self):
+        from b200attn import chunked_prefill_batch_b200
+        self.call = chunked_prefill_batch_b200(self.q, self.pool, self.tables, self.prefix, 0,
+                                               prepare=True)
+
+    def step(self):
+        self.call()
+
+    def e2e_step(self):
+        from b200attn import chunked_prefill_batch_b200
+        qs = [q.to(self.device, non_blocking=True) for q in self.q_h]
+        ts = [t.to(self.device, non_blocking=True) for t in self.tables_h]
+        outs = chunked_prefill_batch_b200(qs, self.pool, ts, self.prefix, 0)
+        for o, oh in zip(outs, self.out_h):
+            oh.copy_(o, non_blocking=True)
+
+    def flops(self) -> float:
+        T = self.T
+        return sum(4.0 * H * D * (T * p + T * (T + 1) / 2) for p in self.prefix)
+
+    def bytes(self) -> float:
+        kv = sum((p + self.T) * H * D * 2 * 2 for p in self.prefix)
+        return kv + 2 * self.nseq * self.T * H * D * 2
+
+    def work(self) -> float:
+        return self.flops()
+
+    def h2d_bytes(self):
+        return sum(q.numel() * 2 for q in self.q_h) + sum(t.numel() * 8 for t in self.tables_h)
+
+    def d2h_bytes(self):
+        return sum(o.numel() * 2 for o in self.out_h)
+
+    def config(self, world):
+        return {"workload": self.desc, "seqs_per_gpu": self.nseq, "chunk": self.T, "heads": H,
+                "head_dim": D, "block_size": S, "kv_dtype": "bf16", "accumulate": "f32",
+                "l2": "KV pool %.1f GB per GPU (larger than L2), no flush" % self.kv_gb,
+                "parallelism": f"sequence-sharded dp{world}"}
+
+    def extra(self, ms_max, world, steps):
+        sec = ms_max * 1e-3 / steps
+        return {"prefill_gbs": self.bytes() * world / sec / 1e9,
+                "prefill_tokens_per_s": self.nseq * self.T * world / sec}
+
+
+class ScatterWorkload:
+    """Slot-mapping scatter of 16 x 512 prefill tokens into a bf16 pool."""
+
+    bound, unit = "hbm", "GB/s"
+
+    def __init__(self, rank, device, n=16 * 512):
+        self.n, self.device = n, device
+        P = n // S * 8
+        self.k = torch.zeros((1, P, S, H, D), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        g = torch.Generator().manual_seed(rank)
+        self.kn_h = torch.randn((n, H, D), generator=g).to(torch.bfloat16).pin_memory()
+        self.vn_h = torch.randn((n, H, D), generator=g).to(torch.bfloat16).pin_memory()
+        self.slots_h = torch.randperm(P * S, generator=g)[:n].pin_memory()
+        self.kn, self.vn, self.slots = (t.to(device) for t in (self.kn_h, self.vn_h, self.slots_h))
+        self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
+        self.desc = f"slot-mapping KV scatter: {n} tokens x 32 heads x 128 dims, bf16"
+
+    def prepare(self):
+        from b200attn import kv_scatter_b200
+        self.call = kv_scatter_b200(self.kn, self.vn, self.pool, self.slots, 0, prepare=True)
+
+    def step(self):
+        self.call()
+
+    def e2e_step(self):
+        from b200attn import kv_scatter_b200
+        kv_scatter_b200(self.kn_h.to(self.device, non_blocking=True),
+                        self.vn_h.to(self.device, non_blocking=True), self.pool,
+                        self.slots_h.to(self.device, non_blocking=True), 0)
+
+    def work(self) -> float:
+        return self.n * H * D * 2 * (2 + 2) + self.n * 8
+
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.kn_h, self.vn_h, self.slots_h))
+
+    def d2h_bytes(self):
+        return 0
+
+    def config(self, world):
+        return {"workload": self.desc, "tokens_per_gpu": self.n, "heads": H, "head_dim": D,
+                "block_size": S, "kv_dtype": "bf16",
+                "l2": "each step moves %.0f MB; no flush between steps" % (self.work() / 1e6),
+                "parallelism": f"token-sharded dp{world}"}
+
+    def extra(self, ms_max, world, steps):
+        return {}
+
+
+def make_workload(name, rank, device, args):
+    if name in ("cfg4", "cfg3"):
+        return DecodeWorkload(name, rank, device, args.batch, args.ctx)
+    if name == "cfg5-t512":
+        return PrefillWorkload(512, rank, device)
+    if name == "cfg5-t64":
+        return PrefillWorkload(64, rank, device)
+    if name == "scatter":
+        return ScatterWorkload(rank, device)
+    raise SystemExit(f"unknown workload {name}")
 
 
 # ------------------------------------------------------------------ clocks
@@ -137,8 +303,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, indices: list[int]):
-        self.indices = indices
-        self.proc = None
+        self.indices, self.proc, self.lines = indices, None, []
 
     def __enter__(self):
         try:
@@ -150,7 +315,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -164,17 +328,14 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
                 idx = int(parts[0])
-            except ValueError:
-                continue
-            if idx not in self.indices:
-                continue
-            try:
+                if idx not in self.indices:
+                    continue
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
             except ValueError:
@@ -197,57 +358,91 @@ def gpu_indices(world: int) -> list[int]:
 
 
 # ------------------------------------------------------------------ CPU leg
-def cpu_reference_sample(steps: int = 1, warmup: int = 0, requests: int = 1,
-                         ctx: int = 32768) -> dict:
-    """Times the reference decode algorithm (oracle port of
-    paged_attention_batch_online_v1) on the host cores on a bounded sample:
-    `requests` sequences of `ctx` tokens of the bench workload's shape."""
+def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
+    """Times the reference algorithm (its CPU restatement under oracle/) on
+    the host cores, all threads, on a bounded sample of the workload."""
     sys.path.insert(0, str(REPO))
     import oracle
+    from b200attn.ops import decode_bytes
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    H, D, S = 32, 128, 16
-    nb = math.ceil(ctx / S)
     g = torch.Generator().manual_seed(5)
-    k = torch.randn((1, nb * requests, S, H, D), generator=g).to(torch.bfloat16)
-    v = torch.randn((1, nb * requests, S, H, D), generator=g).to(torch.bfloat16)
-    tables = torch.randperm(nb * requests, generator=g).view(requests, nb)
-    lens = torch.full((requests,), ctx, dtype=torch.int64)
-    q = torch.randn((requests, H, D), generator=g)
-    # The reference cannot mix bf16 KV with fp32 q; the port upcasts the
-    # (sample) pool to fp32 first, as the bf16 oracle does.
-    kf, vf = k.float(), v.float()
+    if workload in ("cfg4", "cfg3"):
+        # paged_attention_batch_online_v1 on 4 requests x 32768 tokens (cfg4)
+        # or 8 ragged requests (cfg3); the reference cannot mix bf16 KV with
+        # fp32 q, so the bf16 sample pool is upcast to fp32 first.
+        lens = [32768] * 4 if workload == "cfg4" else \
+            torch.randint(1, 4097, (8,), generator=g).tolist()
+        counts = [math.ceil(n / S) for n in lens]
+        P = sum(counts)
+        kf = torch.randn((1, P, S, H, D), generator=g).to(torch.bfloat16).float()
+        vf = torch.randn((1, P, S, H, D), generator=g).to(torch.bfloat16).float()
+        tables = _tables(counts, torch.randperm(P, generator=g))
+        ctx = torch.tensor(lens)
+        q = torch.randn((len(lens), H, D), generator=g)
+        fn = lambda: oracle.paged_decode_online(q, kf, vf, tables, ctx, 0)
+        work = decode_bytes(lens, H, D, S, kv_bytes=2, q_bytes=2, out_bytes=2)
+        unit = "GB/s"
+        sample = (f"{len(lens)} request(s), contexts {lens if len(lens) < 4 else 'U[1,4096]'},"
+                  " H=32, D=128, S=16, bf16 KV upcast to fp32, paged_attention_batch_online_v1"
+                  " restatement (oracle/)")
+    elif workload.startswith("cfg5"):
+        T = 512 if workload.endswith("512") else 64
+        prefix = [2016, 1024]
+        k_pool = torch.randn((1, sum(math.ceil((p + T) / S) for p in prefix), S, H, D),
+                             generator=g).to(torch.bfloat16).float()
+        v_pool = torch.randn_like(k_pool)
+        qs = [torch.randn((T, H, D), generator=g) for _ in prefix]
+        tables, nxt = [], 0
+        for p in prefix:
+            c = math.ceil((p + T) / S)
+            tables.append(list(range(nxt, nxt + c)))
+            nxt += c
+
+        def fn():
+            for q, t, p in zip(qs, tables, prefix):
+                oracle.prefix_prefill_from_pool(q, k_pool, v_pool, t, p, 0)
+        work = sum(4.0 * H * D * (T * p + T * (T + 1) / 2) for p in prefix)
+        unit = "TFLOP/s"
+        sample = (f"2 sequences (prefix 2016 and 1024, chunk {T}), H=32, D=128, fp32, SDPA v2"
+                  " prefill restatement (oracle/)")
+    else:
+        n = 2048
+        k_pool = torch.zeros((1, n // S * 8, S, H, D), dtype=torch.bfloat16)
+        v_pool = torch.zeros_like(k_pool)
+        kn = torch.randn((n, H, D), generator=g).to(torch.bfloat16)
+        slots = torch.randperm(k_pool.shape[1] * S, generator=g)[:n].tolist()
+        fn = lambda: oracle.kv_scatter(k_pool, v_pool, kn, kn, slots, 0)
+        work = n * H * D * 2 * 4 + n * 8
+        unit = "GB/s"
+        sample = f"{n} tokens, per-token KVBlockPool.write_layer loop restatement (oracle/)"
     for _ in range(warmup):
-        oracle.paged_decode_online(q, kf, vf, tables, lens, 0)
+        fn()
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
-        oracle.paged_decode_online(q, kf, vf, tables, lens, 0)
+        fn()
         times.append(time.perf_counter() - t0)
-    from b200attn.ops import decode_bytes
-    nbytes = decode_bytes([ctx] * requests, H, D, S, kv_bytes=2, q_bytes=2, out_bytes=2)
-    return {"seconds": times, "bytes": nbytes, "threads": threads,
-            "sample": f"{requests} request(s) x {ctx} tokens, H=32, D=128, S=16, bf16 KV "
-                      f"upcast to fp32, paged_attention_batch_online_v1 restatement (oracle/)"}
+    sec = sum(times) / len(times)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    return {"value": work / sec / scale, "unit": unit, "cores": threads, "kind": "port",
+            "sample": sample, "seconds_per_step": sec}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    r = cpu_reference_sample(steps=args.steps, warmup=args.warmup, requests=1, ctx=32768)
-    sec = sum(r["seconds"]) / len(r["seconds"])
-    gbs = r["bytes"] / sec / 1e9
-    line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "cfg4 sample on host CPU", "context_len": 32768,
-                       "heads": 32, "head_dim": 128, "block_size": 16, "kv_dtype": "bf16"},
-            "decode_tokens_per_s": 1.0 / sec,
-            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": r["threads"],
-                             "kind": "port", "sample": r["sample"]},
-            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0,
+    r = cpu_reference_sample(args.workload, args.steps, args.warmup)
+    line = {"metric": METRIC if args.workload in ("cfg4", "cfg3") else f"{args.workload} {r['unit']}",
+            "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.workload} bounded sample on host CPU",
+                       "sample": r["sample"]},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -256,15 +451,13 @@ def run_reference(args, rank: int, world: int) -> None:
 def traffic_from_profile(workload: str) -> float | None:
     p = REPO / "profiles" / f"paged_decode_{workload}_traffic.json"
     try:
-        d = json.loads(p.read_text())
-        return float(d["dram_bytes_per_launch_full_size"])
+        return float(json.loads(p.read_text())["dram_bytes_per_launch_full_size"])
     except Exception:
         return None
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch.distributed as dist
-    from b200attn import paged_attention_batch_b200
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -272,17 +465,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if pg:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    wl = Workload(args.workload, rank, world, dev, args.batch, args.ctx)
+    wl = make_workload(args.workload, rank, dev, args)
     stream = torch.cuda.current_stream(dev)
-
-    def step(q, k_new, v_new, tables, ctx, slots, out):
-        return paged_attention_batch_b200(q, wl.pool, tables, ctx, 0, k_new=k_new, v_new=v_new,
-                                          slot_mapping=slots, out=out)
-
-    out = torch.empty((wl.B, wl.H, wl.D), dtype=wl.q_dtype, device=dev)
     with torch.inference_mode():
+        wl.prepare()
         for _ in range(args.warmup):
-            step(wl.q, wl.k_new, wl.v_new, wl.tables, wl.ctx, wl.slots, out)
+            wl.step()
         torch.cuda.synchronize(dev)
         if pg:
             dist.barrier()
@@ -291,73 +479,64 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         with ClockSampler(gpu_indices(world)) as clocks:
             ev0.record(stream)
             for _ in range(args.steps):
-                step(wl.q, wl.k_new, wl.v_new, wl.tables, wl.ctx, wl.slots, out)
+                wl.step()
             ev1.record(stream)
             torch.cuda.synchronize(dev)
         ms = ev0.elapsed_time(ev1)
         if pg:
             dist.barrier()
-        # End to end through the public API with host buffers: H2D of the
-        # step's inputs from pinned memory, the call, D2H of the output and a
-        # host synchronisation every step.
-        torch.cuda.synchronize(dev)
+        # End to end through the public API: H2D of the step's inputs from
+        # pinned memory, the call, D2H of the result, host synchronisation.
+        for _ in range(2):
+            wl.e2e_step()
+        stream.synchronize()
         if pg:
             dist.barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            q = wl.q_h.to(dev, non_blocking=True)
-            kn = wl.knew_h.to(dev, non_blocking=True)
-            vn = wl.vnew_h.to(dev, non_blocking=True)
-            tb = wl.tables_h.to(dev, non_blocking=True)
-            cx = wl.lens_h.to(dev, non_blocking=True)
-            sl = wl.slots_h.to(dev, non_blocking=True)
-            o = step(q, kn, vn, tb, cx, sl, None)
-            wl.out_h.copy_(o, non_blocking=True)
+            wl.e2e_step()
             stream.synchronize()
         e2e_s = time.perf_counter() - t0
     times = torch.tensor([ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
     if pg:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms_max, e2e_ms_max = float(times[0]), float(times[1])
-    clock = clocks.summary()
-    bytes_step = wl.bytes_per_step()
-    per_launch_ms = ms / args.steps  # this rank's own kernel time
-    achieved = bytes_step / (per_launch_ms * 1e-3) / 1e9
-    peak, peak_src = measured_peak()
-    value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
-    e2e_value = bytes_step * world * args.steps / (e2e_ms_max * 1e-3) / 1e9
-    tok_s = wl.B * world * args.steps / (ms_max * 1e-3)
+    scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
+    value = wl.work() * world * args.steps / (ms_max * 1e-3) / scale
+    e2e_value = wl.work() * world * args.steps / (e2e_ms_max * 1e-3) / scale
+    per_launch_s = ms * 1e-3 / args.steps  # this rank's own kernel time
+    if wl.bound == "tensor":
+        peak, src = measured_peak("bf16_tflops")
+        achieved, r_unit = wl.flops() / per_launch_s / 1e12, "TFLOP/s"
+    else:
+        peak, src = measured_peak("hbm_gbs")
+        nbytes = wl.bytes() if hasattr(wl, "bytes") else wl.work()
+        achieved, r_unit = nbytes / per_launch_s / 1e9, "GB/s"
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        r = cpu_reference_sample(steps=1, warmup=0, requests=1, ctx=32768)
-        sec = sum(r["seconds"]) / len(r["seconds"])
-        cpu = {"value": r["bytes"] / sec / 1e9, "unit": "GB/s", "cores": r["threads"],
-               "kind": "port", "sample": r["sample"]}
-    traffic = traffic_from_profile(args.workload)
+        cpu = cpu_reference_sample(args.workload, steps=3, warmup=0)
+        cpu.pop("seconds_per_step")
     if rank == 0:
+        if isinstance(wl, DecodeWorkload):
+            metric = METRIC
+        elif isinstance(wl, PrefillWorkload):
+            metric = f"{args.workload} chunked prefill attention {wl.unit}"
+        else:
+            metric = f"{args.workload} KV scatter {wl.unit}"
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": wl.desc, "batch_per_gpu": wl.B, "global_batch": wl.B * world,
-                       "context_lens": str(wl.lens[0]) if args.workload == "cfg4" else "U[1,4096]",
-                       "heads": wl.H, "head_dim": wl.D, "block_size": wl.S,
-                       "kv_dtype": "bf16", "q_dtype": "bf16", "accumulate": "f32",
-                       "fused_kv_write": True,
-                       "l2": "inputs larger than L2 (KV pool %.1f GB per GPU), no flush"
-                             % (2 * wl.k.numel() * wl.k.element_size() / 1e9),
-                       "parallelism": f"request-sharded dp{world} (no data-path collective)"},
-            "pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
-            "decode_tokens_per_s": tok_s,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_source": peak_src,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": bytes_step},
+            "dtype": "bf16", "data": "synthetic", "config": wl.config(world),
+            **wl.extra(ms_max, world, args.steps),
+            "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
+                         "frac": achieved / peak, "peak_source": src,
+                         "traffic": traffic_from_profile(args.workload),
+                         "algorithmic_per_launch": wl.work()},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": wl.h2d_bytes(),
-                    "d2h_bytes_per_step": wl.out_h.numel() * wl.out_h.element_size(),
-                    "ms_per_step": e2e_ms_max / args.steps},
-            "clocks": clock,
+            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
+                    "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms_max / args.steps},
+            "clocks": clocks.summary(),
             "gpu_launches": args.steps,
         }
         print(json.dumps(line), flush=True)
@@ -367,15 +546,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
 
 def main():
-    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("cfg4", "cfg3"), default="cfg4")
+    ap.add_argument("--workload", default="cfg4",
+                    choices=("cfg4", "cfg3", "cfg5-t512", "cfg5-t64", "scatter"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="requests per GPU (default: the workload's; smaller for profiling)")
+                    help="decode requests per GPU (default: the workload's; smaller for profiling)")
     ap.add_argument("--ctx", type=int, default=None,
                     help="context length of cfg4 requests (default 32768)")
     args = ap.parse_args()

@@ -90,6 +90,31 @@ class _Workspace:
 _WORKSPACE = _Workspace()
 
 
+class PreparedCall:
+    """One op with its C argument struct built once (``prepare=True``).
+
+    Calling it launches the op on the device's current stream and returns
+    the op's result tensor(s).  It keeps every tensor the struct points to
+    alive and owns a private split-K workspace, so repeated calls cost one
+    ctypes call each; calls of one PreparedCall must not overlap on the GPU.
+    """
+
+    def __init__(self, fn, args, device: torch.device, result, what: str, keep=()):
+        self._fn, self._args, self._device = fn, args, device
+        self._result, self._what, self._keep = result, what, keep
+        self._ref = ctypes.byref(args)
+
+    def __call__(self):
+        _lib.check(self._fn(self._ref, _stream_ptr(self._device)), self._what)
+        return self._result
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int, private: bool):
+    if private:
+        return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device) if nbytes else None
+    return _WORKSPACE.get(device, stream, nbytes)
+
+
 def _index_tensor(x, device: torch.device, name: str) -> torch.Tensor:
     if isinstance(x, torch.Tensor):
         if x.dtype not in _INDEX:
@@ -107,7 +132,7 @@ def paged_attention_batch_b200(q: torch.Tensor, pool, block_tables: torch.Tensor
                                slot_mapping: torch.Tensor | None = None,
                                status: torch.Tensor | None = None,
                                out: torch.Tensor | None = None,
-                               max_splits: int = 0) -> torch.Tensor:
+                               max_splits: int = 0, prepare: bool = False):
     """One batched paged decode-attention launch (optionally fused KV write).
 
     q: [B, H, D] (any strides); pool.k / pool.v: contiguous [L, P, S, H, D];
@@ -115,7 +140,8 @@ def paged_attention_batch_b200(q: torch.Tensor, pool, block_tables: torch.Tensor
     context_lengths: [B] (>= 1, including the token being decoded).
     When k_new / v_new ([B, H, D]) and slot_mapping ([B]) are given, they are
     written into the pool first (the caller must then NOT write them itself).
-    Returns a fresh [B, H, D] tensor of q.dtype (or fills ``out``).
+    Returns a fresh [B, H, D] tensor of q.dtype (or fills ``out``); with
+    prepare=True returns a PreparedCall that launches it.
     """
     lib = _lib.load()
     if not q.is_cuda:
@@ -188,19 +214,22 @@ def paged_attention_batch_b200(q: torch.Tensor, pool, block_tables: torch.Tensor
     stream = _stream_ptr(dev)
     nbytes = lib.b200_paged_decode_workspace_size(
         b, h, d, block_tables.shape[1], pool.block_size, pstruct.dtype, max_splits)
-    ws = _WORKSPACE.get(dev, stream, nbytes)
+    ws = _workspace(dev, stream, nbytes, prepare)
     if ws is not None:
         args.workspace = ws.data_ptr()
         args.workspace_bytes = ws.numel()
     args.max_splits_hint = max_splits
     if status is not None:
         args.status = status.data_ptr()
-    _lib.check(lib.b200_paged_decode(ctypes.byref(args), stream), "paged decode")
-    return out
+    call = PreparedCall(lib.b200_paged_decode, args, dev, out, "paged decode",
+                        (q, pool.k, pool.v, block_tables, context_lengths, k_new, v_new,
+                         slot_mapping, status, ws, out))
+    return call if prepare else call()
 
 
 def kv_scatter_b200(k: torch.Tensor, v: torch.Tensor, pool, slot_mapping,
-                    layer_idx: int, *, status: torch.Tensor | None = None) -> None:
+                    layer_idx: int, *, status: torch.Tensor | None = None,
+                    prepare: bool = False):
     """pool[layer, slot // S, slot % S] = k / v for each of the N tokens.
 
     k, v: [N, H, D] (any strides, any float dtype; converted to the pool's);
@@ -239,7 +268,9 @@ def kv_scatter_b200(k: torch.Tensor, v: torch.Tensor, pool, slot_mapping,
     args.slot_dtype = _INDEX[slots.dtype]
     if status is not None:
         args.status = status.data_ptr()
-    _lib.check(lib.b200_kv_scatter(ctypes.byref(args), _stream_ptr(dev)), "kv scatter")
+    call = PreparedCall(lib.b200_kv_scatter, args, dev, None, "kv scatter",
+                        (k, v, pool.k, pool.v, slots, status))
+    return call if prepare else call()
 
 
 def _prefill_struct(q, pool, pstruct, table, prefix_len, layer_idx, out, status):
@@ -284,7 +315,7 @@ def _check_prefill_inputs(q, pool, prefix_len, layer_idx):
 
 def chunked_prefill_b200(q: torch.Tensor, pool, block_table, prefix_len: int,
                          layer_idx: int, *, out: torch.Tensor | None = None,
-                         status: torch.Tensor | None = None) -> torch.Tensor:
+                         status: torch.Tensor | None = None, prepare: bool = False):
     """Prefix-aware causal attention of one prefill chunk over paged KV.
 
     q: [T, H, D] (any strides) for absolute positions prefix_len .. prefix_len+T-1;
@@ -311,18 +342,19 @@ def chunked_prefill_b200(q: torch.Tensor, pool, block_table, prefix_len: int,
     stream = _stream_ptr(dev)
     nbytes = lib.b200_chunked_prefill_workspace_size(t, h, d, table.shape[0],
                                                      pool.block_size, pstruct.dtype)
-    ws = _WORKSPACE.get(dev, stream, nbytes)
+    ws = _workspace(dev, stream, nbytes, prepare)
     if ws is not None:
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
-    _lib.check(lib.b200_chunked_prefill(ctypes.byref(a), stream), "chunked prefill")
-    return out
+    call = PreparedCall(lib.b200_chunked_prefill, a, dev, out, "chunked prefill",
+                        (q, pool.k, pool.v, table, status, ws, out))
+    return call if prepare else call()
 
 
 def chunked_prefill_batch_b200(qs: Sequence[torch.Tensor], pool, block_tables: Sequence,
                                prefix_lens: Sequence[int], layer_idx: int, *,
                                outs: Sequence[torch.Tensor] | None = None,
-                               status: torch.Tensor | None = None) -> list[torch.Tensor]:
+                               status: torch.Tensor | None = None, prepare: bool = False):
     """Several independent prefill chunks (same pool and layer) in one call."""
     lib = _lib.load()
     if not (len(qs) == len(block_tables) == len(prefix_lens)):
@@ -349,14 +381,16 @@ def chunked_prefill_batch_b200(qs: Sequence[torch.Tensor], pool, block_tables: S
         total_ws = max(total_ws, lib.b200_chunked_prefill_workspace_size(
             q.shape[0], q.shape[1], q.shape[2], table.shape[0], pool.block_size, pstruct.dtype))
     stream = _stream_ptr(dev)
-    ws = _WORKSPACE.get(dev, stream, total_ws)
+    ws = _workspace(dev, stream, total_ws, prepare)
     if ws is not None:
         for i in range(len(qs)):
             structs[i].workspace = ws.data_ptr()
             structs[i].workspace_bytes = ws.numel()
     batch = _lib.PrefillBatchArgs(len(qs), structs)
-    _lib.check(lib.b200_chunked_prefill_batch(ctypes.byref(batch), stream), "chunked prefill")
-    return results
+    call = PreparedCall(lib.b200_chunked_prefill_batch, batch, dev, results, "chunked prefill",
+                        (tuple(qs), pool.k, pool.v, tuple(keep), status, ws, tuple(results),
+                         structs))
+    return call if prepare else call()
 
 
 def decode_bytes(context_lengths: Sequence[int], num_heads: int, head_dim: int,

@@ -1,24 +1,28 @@
 // prefill_tc.cu -- prefix-aware chunked-prefill attention on tcgen05 tensor
 // cores (bf16 KV pool, head_dim 64 or 128, block size >= 8).
 //
-// One CTA per (sequence, head, tile of 128 queries).  Query i of a chunk sits
-// at absolute position prefix_len + i and attends to keys 0 .. prefix_len + i
-// (minivllm/attention.py:256-265), all read from the paged pool.
+// One CTA per (sequence, head, pair of 128-query tiles).  Query i of a chunk
+// sits at absolute position prefix_len + i and attends to keys
+// 0 .. prefix_len + i (minivllm/attention.py:256-265), all read from the
+// paged pool.  The two query tiles share every K/V tile and ping-pong on the
+// tensor core: while one softmax group works on its scores, the MMAs of the
+// other group run.
 //
-// Warp roles (6 warps):
+// Warp roles (10 warps):
 //   warp 0   TMA producer: for each 128-key tile walks the block table and
 //            loads, per KV block, boxes {64 d, 1 head, rbox rows} of K and V
 //            with 128-byte swizzle into a 2-stage ring of this CTA.
-//   warp 1   TMEM allocation (256 columns) and the MMA issuer (one thread):
-//              S   = Q K^T   -> TMEM columns [0, 128)         (M=128,N=128)
-//              O  += P V     -> TMEM columns [128, 128+D)      (M=128,N=D)
+//   warp 1   TMEM allocation (512 columns) and the MMA issuer (one thread):
+//              S_w  = Q_w K^T -> TMEM columns [128w, 128w+128)   (M=128,N=128)
+//              O_w += P_w V   -> TMEM columns [256+128w, +D)     (M=128,N=D)
 //            Q, K and P are K-major SW128 operands; V is read MN-major.
-//   warps 2-5 softmax / correction / epilogue: thread r of the warpgroup owns
-//            query row r = TMEM lane r: it loads its S row (tcgen05.ld),
-//            applies the causal mask on absolute positions, updates the
-//            running max/sum in the log2 domain, rescales its O row in TMEM
-//            when the max grew, and writes its bf16 P row into the swizzled
-//            smem tile that the P.V MMA reads.
+//   warps 2-5, 6-9  softmax / correction / epilogue of query tile 0 / 1:
+//            thread r of a group owns query row r = TMEM lane r: two passes
+//            over its S row (tcgen05.ld) give the masked row max, then the
+//            probabilities; the running max is kept unless it grows by more
+//            than 2^8 (lazy rescale of O in TMEM); the bf16 P row is written
+//            over the S columns already consumed, and the P.V MMA reads it
+//            from TMEM as its A operand.
 // V rows beyond the last valid key of the last tile are zeroed in smem
 // before the P.V MMA: unwritten pool rows can hold NaN and 0 * NaN is NaN
 // inside the tensor core as well (minivllm/paged_attention_batch.py:234-240).
@@ -39,8 +43,8 @@ namespace b200 {
 namespace {
 
 constexpr int kMaxSeqs = 128;  // sequences per launch (host splits larger batches)
-constexpr int kThreads = 192;
-constexpr int kBM = 128;       // queries per CTA
+constexpr int kThreads = 320;  // producer, MMA, two 4-warp softmax groups
+constexpr int kBM = 128;       // queries per query tile (two tiles per CTA)
 constexpr int kBN = 128;       // keys per tile
 
 struct SeqDesc {
@@ -60,6 +64,7 @@ struct PrefillParams {
   int64_t P, S, H, D;
   int64_t layer;
   int32_t q_dtype, out_dtype, table_i64;
+  int32_t q_vec, out_vec;  // 16-byte row access is legal for every sequence
   int32_t rbox, rb_shift, s_shift;
   int32_t nseq;
   int32_t max_qtiles;
@@ -92,6 +97,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Same with the A operand (M x K, bf16 pairs per 32-bit column) in TMEM.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -144,11 +160,29 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Hardware base-2 exponential (MUFU), flushing denormal results to zero.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -165,14 +199,54 @@ __device__ __forceinline__ uint32_t sw128(int r, int ch) {
 // Shared-memory layout (offsets from a 1024-aligned base).
 template <int D>
 struct Smem {
-  static constexpr int HALVES = D / 64;           // 64-element (128-byte) column halves
+  static constexpr int HALVES = D / 64;            // 64-element (128-byte) column halves
   static constexpr int TILE = HALVES * 128 * 128;  // one 128-row operand tile
-  static constexpr int Q = 0;
-  static constexpr int K0 = Q + TILE;              // K stage 0, K stage 1
+  static constexpr int Q0 = 0;                     // Q tiles 0 and 1
+  static constexpr int K0 = Q0 + 2 * TILE;         // K stage 0, K stage 1
   static constexpr int V0 = K0 + 2 * TILE;         // V stage 0, V stage 1
-  static constexpr int PT = V0 + 2 * TILE;         // P tile: 128 x 128 bf16
-  static constexpr int BAR = PT + 2 * 128 * 128;
+  static constexpr int BAR = V0 + 2 * TILE;
   static constexpr int BYTES = BAR + 256;
+};
+
+// Loads query row i (zeros past T) of head h into row r of a swizzled Q tile.
+template <int D>
+__device__ __forceinline__ void load_q_row(uint8_t* tile, int r, int i, int h, const SeqDesc& sd,
+                                           int q_dtype, int q_vec) {
+  constexpr int HALVES = D / 64;
+#pragma unroll
+  for (int half = 0; half < HALVES; ++half) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const int d0 = half * 64 + ch * 8;
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (i < sd.T) {
+        const int64_t off = i * sd.qs0 + h * sd.qs1 + d0 * sd.qs2;
+        if (q_vec && q_dtype == B200_DTYPE_BF16) {
+          w = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(sd.q) + off);
+        } else if (q_vec && q_dtype == B200_DTYPE_F32) {
+          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(sd.q) + off);
+          const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(sd.q) + off + 4);
+          w = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
+                         pack_bf16(b.z, b.w));
+        } else {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = load_elem(sd.q, off + e * sd.qs2, q_dtype);
+          w = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
+                         pack_bf16(f[6], f[7]));
+        }
+      }
+      *reinterpret_cast<uint4*>(tile + half * 16384 + sw128(r, ch)) = w;
+    }
+  }
+}
+
+// Per-CTA bookkeeping shared by the roles.
+struct Geom {
+  int i0;          // first query of the CTA
+  int nkt[2];      // key tiles of query tile 0 / 1 (0 = tile inactive)
+  int nmax;        // max(nkt)
+  int64_t total;   // keys any query of the CTA may see
 };
 
 template <int D>
@@ -187,33 +261,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int seq = blockIdx.y;
   const int h = blockIdx.x % static_cast<int>(p.H);
-  const int qt = blockIdx.x / static_cast<int>(p.H);
+  const int qp = blockIdx.x / static_cast<int>(p.H);
   const SeqDesc& sd = p.seq[seq];
-  const int i0 = qt * kBM;
-  if (i0 >= sd.T) return;
+  Geom g;
+  g.i0 = qp * 2 * kBM;
+  if (g.i0 >= sd.T) return;
   const int64_t prefix = sd.prefix;
-  const int q_hi = min(sd.T, i0 + kBM);                // queries [i0, q_hi)
-  const int64_t total = prefix + q_hi;                   // keys this CTA may see
-  const int nkt = static_cast<int>((total + kBN - 1) / kBN);
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const int lo = g.i0 + w * kBM;
+    const int hi = min(sd.T, lo + kBM);
+    g.nkt[w] = lo < sd.T ? static_cast<int>((prefix + hi + kBN - 1) / kBN) : 0;
+  }
+  g.nmax = max(g.nkt[0], g.nkt[1]);
+  g.total = prefix + min(sd.T, g.i0 + 2 * kBM);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* kv_full = bars + 0;   // [2]
   uint64_t* kv_empty = bars + 2;  // [2]
-  uint64_t* s_full = bars + 4;
-  uint64_t* p_full = bars + 5;
-  uint64_t* o_done = bars + 6;
-  uint64_t* mma_idle = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
-  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 9);
+  uint64_t* s_full = bars + 4;    // [2] per query tile
+  uint64_t* p_full = bars + 6;    // [2]
+  uint64_t* o_done = bars + 8;    // [2]
+  uint64_t* mma_idle = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 12);
 
   if (threadIdx.x == 0) {
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
+    }
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -221,41 +301,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(256)
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Q tile: softmax thread r loads query row i0 + r (zeros past T) into the
-  // swizzled K-major tile, converting to bf16.
-  if (warp >= 2) {
-    // Row r of every 128-row tile is TMEM lane r; a warp may only touch the
-    // 32 lanes [32*(warp%4), +32), so rows follow (warp % 4, lane).
-    const int r = (warp & 3) * 32 + lane;
-    const int i = i0 + r;
-    uint8_t* qt_base = smem + L::Q;
-#pragma unroll
-    for (int half = 0; half < L::HALVES; ++half) {
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        float f[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int d = half * 64 + ch * 8 + e;
-          f[e] = (i < sd.T) ? load_elem(sd.q, i * sd.qs0 + h * sd.qs1 + d * sd.qs2, p.q_dtype) : 0.f;
-        }
-        uint4 w = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
-                             pack_bf16(f[6], f[7]));
-        *reinterpret_cast<uint4*>(qt_base + half * 16384 + sw128(r, ch)) = w;
-      }
-    }
-    fence_proxy_async_shared();
-  }
+  // Q tiles: softmax group w loads query tile w; row r of a 128-row tile is
+  // TMEM lane r, and a warp may only touch lanes [32*(warp%4), +32), so rows
+  // follow (warp % 4, lane).
+  const int wg = warp >= 2 ? (warp - 2) >> 2 : -1;  // softmax group of this warp
+  const int r = (warp & 3) * 32 + lane;             // row within the group's tile
+  if (wg >= 0)
+    load_q_row<D>(smem + L::Q0 + wg * L::TILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
+  fence_proxy_async_shared();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem;        // columns [0, 128)
-  const uint32_t tmem_o = tmem + 128;  // columns [128, 128 + D)
+  // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).
+  auto tmem_s = [&](int w) { return tmem + static_cast<uint32_t>(w * 128); };
+  auto tmem_o = [&](int w) { return tmem + 256u + static_cast<uint32_t>(w * 128); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -264,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int64_t j_base = -(int64_t(1) << 40);
     int64_t my_entry = 0;
     int issued = 0;
-    for (int j = 0; j < nkt; ++j) {
+    for (int j = 0; j < g.nmax; ++j) {
       const int st = j & 1;
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1) ? 1 : 0;
@@ -278,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int64_t key0 = static_cast<int64_t>(j) * kBN;
       const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
-                                          (total - key0 + p.rbox - 1) >> p.rb_shift));
+                                          (g.total - key0 + p.rbox - 1) >> p.rb_shift));
       if (lane == 0)
         mbar_arrive_expect_tx(&kv_full[st], static_cast<uint32_t>(nb * 2 * L::HALVES * box_bytes));
       uint8_t* kdst = smem + L::K0 + st * L::TILE;
@@ -322,45 +386,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(128, 128, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
-      const uint32_t q_addr = smem_u32(smem + L::Q);
-      const uint32_t p_addr = smem_u32(smem + L::PT);
       bool ok = true;
-      auto issue_s = [&](int j) -> bool {
+      auto issue_s = [&](int w, int j) -> bool {
         const int st = j & 1;
         if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + L::Q0 + w * L::TILE);
         const uint32_t k_addr = smem_u32(smem + L::K0 + st * L::TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16(tmem_s, smem_desc_sw128(q_addr + koff, 16, 1024),
+          mma_bf16(tmem_s(w), smem_desc_sw128(q_addr + koff, 16, 1024),
                    smem_desc_sw128(k_addr + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(s_full);
+        mma_commit(&s_full[w]);
         return true;
       };
-      ok = issue_s(0);
-      for (int j = 0; ok && j < nkt; ++j) {
-        if (!mbar_wait(p_full, j & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      for (int w = 0; ok && w < 2; ++w)
+        if (g.nkt[w] > 0) ok = issue_s(w, 0);
+      for (int j = 0; ok && j < g.nmax; ++j) {
         const int st = j & 1;
         const uint32_t v_addr = smem_u32(smem + L::V0 + st * L::TILE);
+        for (int w = 0; ok && w < 2; ++w) {
+          if (j >= g.nkt[w]) continue;
+          if (!mbar_wait(&p_full[w], j & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // P (bf16 pairs over S_w's first 64 columns) is the TMEM A operand;
+          // 16 keys per step = 8 columns.  MMAs of this thread execute in
+          // issue order, so S_w of the next tile is written only after this
+          // P.V has read P.
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16(tmem_o, smem_desc_sw128(p_addr + poff, 16, 1024),
-                   smem_desc_sw128(v_addr + kk * 2048, 16384, 1024), idesc_o,
-                   (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_bf16_ts(tmem_o(w), tmem_s(w) + kk * 8,
+                        smem_desc_sw128(v_addr + kk * 2048, 16384, 1024), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&o_done[w]);
+          if (j + 1 < g.nkt[w] && !issue_s(w, j + 1)) ok = false;
         }
-        mma_commit(&kv_empty[st]);
-        mma_commit(o_done);
-        if (j + 1 < nkt && !issue_s(j + 1)) {
-          ok = false;
-          break;
-        }
+        if (ok) mma_commit(&kv_empty[st]);
       }
       if (!ok) {
         report(p.status, B200_DEV_WAIT_TIMEOUT);
@@ -373,108 +439,152 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = (warp & 3) * 32 + lane;    // query row == TMEM lane
+    const int w = wg;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const int i = min(i0 + r, sd.T - 1);     // rows past T mirror the last query
+    const int iq = g.i0 + w * kBM + r;                 // this thread's query
+    const int i = min(iq, sd.T - 1);                   // rows past T mirror the last query
     const int64_t qpos = prefix + i;
+    // A warp whose 32 rows are all past T has nothing to compute (its rows of
+    // P and O are never used); it only keeps the barrier protocol.
+    const bool warp_live = g.i0 + w * kBM + (warp & 3) * 32 < sd.T;
+    const int nkt = g.nkt[w];
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(s_full, j & 1)) {
+      if (!mbar_wait(&s_full[w], j & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s + lane_base + c, s + c);
-      tmem_wait_ld();
       const int64_t key0 = static_cast<int64_t>(j) * kBN;
-      float mx = -INFINITY;
-      if (key0 + kBN - 1 <= qpos) {
+      const bool need_mask = key0 + kBN - 1 > prefix + g.i0 + w * kBM;  // some key may be masked
+      float alpha = 1.f, m_use = m;
+      bool rescale = false;
+      // Keys c <= lim of this tile are visible to this row (int32, clamped).
+      const int lim = static_cast<int>(max(min(qpos - key0, static_cast<int64_t>(kBN - 1)),
+                                           static_cast<int64_t>(-1)));
+      if (warp_live) {
+        // Pass 1: row max of the masked raw scores (the scale is positive, so
+        // it is applied once to the max).
+        float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          s[c] *= p.scale_log2;
-          mx = fmaxf(mx, s[c]);
+        for (int c = 0; c < kBN; c += 32) {
+          float sv[32];
+          tmem_ld32(tmem_s(w) + lane_base + c, sv);
+          tmem_wait_ld();
+          if (!need_mask) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, c + e <= lim ? sv[e] : -INFINITY);
+          }
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          s[c] = (key0 + c <= qpos) ? s[c] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
-        }
+        mx *= p.scale_log2;
+        // Lazy rescale: keep the old max unless the new one exceeds it by
+        // more than 8 (probabilities then stay below 2^8, exact in fp32).
+        if (mx > m + 8.f) m_use = mx;
+        rescale = __any_sync(0xffffffffu, m_use != m) && j > 0;
+        alpha = ex2_approx(m - m_use);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = fast_exp2(m - m_new);
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        s[c] = fast_exp2(s[c] - m_new);
-        rs += s[c];
-      }
-      l = l * alpha + rs;
-      m = m_new;
       if (j > 0) {
-        // P.V of the previous tile must be done before O is rescaled and
-        // before the P tile is overwritten.
-        if (!mbar_wait(o_done, (j - 1) & 1)) {
+        // O is stable once the previous P.V completed.
+        if (!mbar_wait(&o_done[w], (j - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (warp_live && rescale) {
 #pragma unroll
           for (int c = 0; c < D; c += 32) {
             float o[32];
-            tmem_ld32(tmem_o + lane_base + c, o);
+            tmem_ld32(tmem_o(w) + lane_base + c, o);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(tmem_o + lane_base + c, o);
+            tmem_st32(tmem_o(w) + lane_base + c, o);
           }
-          tmem_wait_st();
         }
       }
-      // Zero V rows past the last valid key of the tile (pool rows there may
-      // be unwritten); thread r clears row r of both column halves.
-      const int64_t valid = total - key0;
-      if (valid < kBN && r >= valid) {
+      if (warp_live) {
+        // Pass 2: probabilities (packed FMA for the exponent argument and the
+        // row sum), bf16 pairs written over the S columns already consumed
+        // (chunk c -> P columns [c/2, c/2 + 16)).
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nm2 = make_float2(-m_use, -m_use);
+        const float2 one2 = make_float2(1.f, 1.f);
+        float2 rs2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < kBN; c += 32) {
+          float sv[32];
+          tmem_ld32(tmem_s(w) + lane_base + c, sv);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 a = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nm2);
+            float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
+            if (need_mask) {
+              p0 = c + e <= lim ? p0 : 0.f;
+              p1 = c + e + 1 <= lim ? p1 : 0.f;
+            }
+            rs2 = ffma2(make_float2(p0, p1), one2, rs2);
+            pk[e >> 1] = pack_bf16(p0, p1);
+          }
+          tmem_st16(tmem_s(w) + lane_base + (c >> 1), pk);
+        }
+        l = l * alpha + (rs2.x + rs2.y);
+        m = m_use;
+      }
+      tmem_wait_st();
+      // Zero V rows past the last valid key of the last tile (pool rows there
+      // may be unwritten); the group issuing the tile's first P.V does it.
+      const int64_t valid = g.total - key0;
+      const int first_w = j < g.nkt[0] ? 0 : 1;
+      if (w == first_w && valid < kBN && r >= valid) {
         uint8_t* vrow = smem + L::V0 + (j & 1) * L::TILE + r * 128;
 #pragma unroll
         for (int half = 0; half < L::HALVES; ++half)
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<uint4*>(vrow + half * 16384 + ch * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vrow + half * 16384 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        fence_proxy_async_shared();
       }
-      uint8_t* pt = smem + L::PT;
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int c = ch * 8;
-        uint4 w = make_uint4(pack_bf16(s[c], s[c + 1]), pack_bf16(s[c + 2], s[c + 3]),
-                             pack_bf16(s[c + 4], s[c + 5]), pack_bf16(s[c + 6], s[c + 7]));
-        *reinterpret_cast<uint4*>(pt + (ch >> 3) * 16384 + sw128(r, ch & 7)) = w;
-      }
-      fence_proxy_async_shared();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[w]);
     }
-    if (ok && !mbar_wait(o_done, (nkt - 1) & 1)) ok = false;
-    if (!ok) {
-      if (r == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
-      *abort_flag = 1;
-    } else {
-      tc_fence_after();
-      const int iq = i0 + r;
-      const float inv = 1.0f / l;
+    if (nkt > 0) {
+      if (ok && !mbar_wait(&o_done[w], (nkt - 1) & 1)) ok = false;
+      if (!ok) {
+        if (r == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
+        *abort_flag = 1;
+      } else if (warp_live) {
+        tc_fence_after();
+        const float inv = 1.0f / l;
+        const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        float o[32];
-        tmem_ld32(tmem_o + lane_base + c, o);
-        tmem_wait_ld();
-        if (iq < sd.T) {
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(tmem_o(w) + lane_base + c, o);
+          tmem_wait_ld();
+          if (iq < sd.T) {
+            const int64_t base = iq * sd.os0 + h * sd.os1 + c * sd.os2;
+            if (vec) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            store_elem(sd.out, iq * sd.os0 + h * sd.os1 + (c + e) * sd.os2, p.out_dtype, o[e] * inv);
+              for (int e = 0; e < 32; e += 8) {
+                const uint4 wv = make_uint4(pack_bf16(o[e] * inv, o[e + 1] * inv),
+                                            pack_bf16(o[e + 2] * inv, o[e + 3] * inv),
+                                            pack_bf16(o[e + 4] * inv, o[e + 5] * inv),
+                                            pack_bf16(o[e + 6] * inv, o[e + 7] * inv));
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(sd.out) + base + e) = wv;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                store_elem(sd.out, base + e * sd.os2, p.out_dtype, o[e] * inv);
+            }
+          }
         }
       }
     }
@@ -483,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
                  : "memory");
   }
 }
@@ -555,6 +665,7 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
     prm.status = a0.status;
     prm.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(D)));
     int64_t max_qt = 0;
+    bool q_vec = true, out_vec = true;
     for (int64_t i = 0; i < cnt; ++i) {
       const b200_prefill_args_t& s = seqs[base + i];
       if (s.block_table_dtype != a0.block_table_dtype)
@@ -575,9 +686,19 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
       d.prefix = static_cast<int32_t>(s.prefix_len);
       d.T = static_cast<int32_t>(s.num_tokens);
       d.table_len = static_cast<int32_t>(std::min<int64_t>(s.block_table_len, INT32_MAX));
-      max_qt = std::max<int64_t>(max_qt, ceil_div(s.num_tokens, kBM));
+      max_qt = std::max<int64_t>(max_qt, ceil_div(s.num_tokens, 2 * kBM));
+      const size_t qes = dtype_size(s.q_dtype);
+      const bool qv = s.q_stride[2] == 1 && (reinterpret_cast<uintptr_t>(s.q) % 16) == 0 &&
+                      (s.q_stride[0] * static_cast<int64_t>(qes)) % 16 == 0 &&
+                      (s.q_stride[1] * static_cast<int64_t>(qes)) % 16 == 0;
+      const bool ov = s.out_stride[2] == 1 && (reinterpret_cast<uintptr_t>(s.out) % 16) == 0 &&
+                      (s.out_stride[0] * 2) % 16 == 0 && (s.out_stride[1] * 2) % 16 == 0;
+      q_vec = q_vec && qv;
+      out_vec = out_vec && ov;
     }
     prm.max_qtiles = static_cast<int32_t>(max_qt);
+    prm.q_vec = q_vec ? 1 : 0;
+    prm.out_vec = out_vec ? 1 : 0;
     const dim3 grid(static_cast<unsigned>(max_qt * H), static_cast<unsigned>(cnt));
     if (D == 128)
       prefill_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
