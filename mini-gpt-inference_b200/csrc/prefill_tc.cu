@@ -323,10 +323,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Every lane issues TMA boxes: a K/V tile is (keys/rbox blocks) x (K, V)
+    // x (D/64 column halves) small boxes, and spreading their issue over the
+    // warp keeps the copy engine fed.
     const int box_bytes = 64 * p.rbox * 2;
     const int boxes_per_tile = kBN / p.rbox;
-    int64_t j_base = -(int64_t(1) << 40);
-    int64_t my_entry = 0;
+    constexpr int PER_BLOCK = 2 * L::HALVES;  // boxes per KV block (K/V x halves)
     int issued = 0;
     for (int j = 0; j < g.nmax; ++j) {
       const int st = j & 1;
@@ -344,32 +346,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
                                           (g.total - key0 + p.rbox - 1) >> p.rb_shift));
       if (lane == 0)
-        mbar_arrive_expect_tx(&kv_full[st], static_cast<uint32_t>(nb * 2 * L::HALVES * box_bytes));
+        mbar_arrive_expect_tx(&kv_full[st], static_cast<uint32_t>(nb * PER_BLOCK * box_bytes));
+      __syncwarp();
       uint8_t* kdst = smem + L::K0 + st * L::TILE;
       uint8_t* vdst = smem + L::V0 + st * L::TILE;
-      for (int b = 0; b < nb; ++b) {
+      for (int it = lane; it < nb * PER_BLOCK; it += 32) {
+        const int b = it / PER_BLOCK;
+        const int sel = it % PER_BLOCK;
+        const int half = sel % L::HALVES;
         const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
         const int64_t blk = key >> p.s_shift;
-        if (blk < j_base || blk >= j_base + 32) {
-          j_base = blk;
-          my_entry = (blk + lane < sd.table_len)
-                         ? load_index(sd.table, (blk + lane) * sd.ts, p.table_i64)
-                         : -1;
-        }
-        int64_t phys = __shfl_sync(0xffffffffu, my_entry, static_cast<int>(blk - j_base));
+        int64_t phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
         if (phys < 0 || phys >= p.P) {
-          if (lane == 0) report(p.status, B200_DEV_BAD_BLOCK);
+          report(p.status, B200_DEV_BAD_BLOCK);
           phys = 0;
         }
-        if (lane == 0) {
-          const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
-#pragma unroll
-          for (int half = 0; half < L::HALVES; ++half) {
-            const uint32_t off = half * 16384 + b * p.rbox * 128;
-            tma_load_3d(kdst + off, &tmk, &kv_full[st], half * 64, h, row);
-            tma_load_3d(vdst + off, &tmv, &kv_full[st], half * 64, h, row);
-          }
-        }
+        const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
+        const uint32_t off = half * 16384 + b * p.rbox * 128;
+        if (sel < L::HALVES)
+          tma_load_3d(kdst + off, &tmk, &kv_full[st], half * 64, h, row);
+        else
+          tma_load_3d(vdst + off, &tmv, &kv_full[st], half * 64, h, row);
       }
       ++issued;
     }
@@ -467,17 +464,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Pass 1: row max of the masked raw scores (the scale is positive, so
         // it is applied once to the max).
         float mx = -INFINITY;
+        {
+          float sv[kBN];  // one TMEM round trip for the whole row
 #pragma unroll
-        for (int c = 0; c < kBN; c += 32) {
-          float sv[32];
-          tmem_ld32(tmem_s(w) + lane_base + c, sv);
+          for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s(w) + lane_base + c, sv + c);
           tmem_wait_ld();
           if (!need_mask) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
+            for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, sv[e]);
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, c + e <= lim ? sv[e] : -INFINITY);
+            for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, e <= lim ? sv[e] : -INFINITY);
           }
         }
         mx *= p.scale_log2;
@@ -515,13 +512,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float2 one2 = make_float2(1.f, 1.f);
         float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < kBN; c += 32) {
-          float sv[32];
+        for (int c = 0; c < kBN; c += 64) {
+          float sv[64];  // two chunks per TMEM round trip
           tmem_ld32(tmem_s(w) + lane_base + c, sv);
+          tmem_ld32(tmem_s(w) + lane_base + c + 32, sv + 32);
           tmem_wait_ld();
-          uint32_t pk[16];
+          uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
+          for (int e = 0; e < 64; e += 2) {
             const float2 a = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nm2);
             float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
             if (need_mask) {
@@ -531,7 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             rs2 = ffma2(make_float2(p0, p1), one2, rs2);
             pk[e >> 1] = pack_bf16(p0, p1);
           }
+          // Chunk [c, c+64) -> P columns [c/2, c/2 + 32): all already read.
           tmem_st16(tmem_s(w) + lane_base + (c >> 1), pk);
+          tmem_st16(tmem_s(w) + lane_base + (c >> 1) + 16, pk + 16);
         }
         l = l * alpha + (rs2.x + rs2.y);
         m = m_use;
