@@ -33,7 +33,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -298,62 +297,72 @@ def make_workload(name, rank, device, args):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clocks and clock-event (throttle) reasons of the GPUs in use
+    every few milliseconds while the timed region runs (NVML, read-only)."""
 
-    def __init__(self, indices: list[int]):
-        self.indices, self.proc, self.lines = indices, None, []
+    def __init__(self, indices: list, period_s: float = 0.002):
+        self.indices, self.period = indices, period_s
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = None
+        self._thread = None
+
+    def _run(self):
+        import pynvml
+        try:
+            handles = []
+            for ident in self.indices:
+                if isinstance(ident, int) or str(ident).isdigit():
+                    handles.append(pynvml.nvmlDeviceGetHandleByIndex(int(ident)))
+                else:
+                    handles.append(pynvml.nvmlDeviceGetHandleByUUID(str(ident)))
+            while not self._stop.is_set():
+                for h in handles:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), float(mx), int(rs)))
+                self._stop.wait(self.period)
+        except Exception:
+            pass
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+            pynvml.nvmlInit()
         except Exception:
-            self.proc = None
+            return self
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=10)
-            except Exception:
-                self.proc.kill()
-                out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         return False
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                idx = int(parts[0])
-                if idx not in self.indices:
-                    continue
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        import pynvml
+        names = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted(n for n, bit in names.items() if any(s[2] & bit for s in self.samples))
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
-def gpu_indices(world: int) -> list[int]:
+def gpu_indices(world: int) -> list:
+    """NVML identifiers (index or UUID) of the GPUs this job's ranks use."""
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
-        ids = [int(x) for x in vis.split(",") if x.strip().isdigit()]
-        return ids[:world] if len(ids) >= world else ids
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        return ids[:world]
     return list(range(world))
 
 

@@ -8,6 +8,8 @@
 // fused QKV projection, minivllm/attention.py:180-191 and :360-368).
 // Semantics: minivllm/attention.py:370-392 (decode) and :193-208 via
 // KVBlockPool.write_layer (minivllm/kv_block_pool.py:91-109) (prefill).
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -85,33 +87,38 @@ __device__ __forceinline__ void read_run(const void* base, int64_t off, int64_t 
     f[i] = (d0 + i < D) ? load_elem(base, off + i * sd, dtype) : 0.f;
 }
 
-// One thread per (token, head, 16-byte chunk of the pool row).
+// One CTA per token: the token's H*D elements form one contiguous run in the
+// pool, and (for q/k/v views of a fused projection) one contiguous run in the
+// source as well, so the CTA copies 16-byte chunks with no index division.
+// Rows whose heads are not contiguous fall back to per-head addressing with
+// 32-bit arithmetic.
 template <typename PoolT>
 __global__ void __launch_bounds__(256) kv_scatter_kernel(const ScatterParams p) {
   constexpr int NE = Pack<PoolT>::N;
-  const int64_t chunks_per_head = (p.D + NE - 1) / NE;
-  const int64_t total = p.N * p.H * chunks_per_head;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t c = i % chunks_per_head;
-    const int64_t nh = i / chunks_per_head;
-    const int64_t h = nh % p.H;
-    const int64_t n = nh / p.H;
-    const int64_t slot = load_index(p.slots, n * p.ss, p.slots_i64);
-    if (slot < 0 || slot >= p.P * p.S) {
-      if (h == 0 && c == 0) report(p.status, B200_DEV_BAD_SLOT);
-      continue;
-    }
-    const int64_t d0 = c * NE;
-    const int64_t dst = ((p.layer_row0 + slot) * p.H + h) * p.D + d0;
+  const int64_t n = blockIdx.x;
+  const int64_t slot = load_index(p.slots, n * p.ss, p.slots_i64);
+  if (slot < 0 || slot >= p.P * p.S) {
+    if (threadIdx.x == 0) report(p.status, B200_DEV_BAD_SLOT);
+    return;
+  }
+  const int D = static_cast<int>(p.D);
+  const int cpr = (D + NE - 1) / NE;               // chunks per head row
+  const int chunks = static_cast<int>(p.H) * cpr;  // chunks per token
+  const bool full_chunks = (D % NE) == 0;
+  const int64_t dst0 = (p.layer_row0 + slot) * p.H * p.D;
+  const int64_t ks0 = n * p.ks0, vs0 = n * p.vs0;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const int h = c / cpr;
+    const int d0 = (c - h * cpr) * NE;
     float fk[NE], fv[NE];
-    read_run<NE>(p.k, n * p.ks0 + h * p.ks1 + d0 * p.ks2, p.ks2, p.in_dtype, p.vec_ok, d0, p.D, fk);
-    read_run<NE>(p.v, n * p.vs0 + h * p.vs1 + d0 * p.vs2, p.vs2, p.in_dtype, p.vec_ok, d0, p.D, fv);
-    if (d0 + NE <= p.D && ((p.D % NE) == 0)) {
+    read_run<NE>(p.k, ks0 + h * p.ks1 + d0 * p.ks2, p.ks2, p.in_dtype, p.vec_ok, d0, p.D, fk);
+    read_run<NE>(p.v, vs0 + h * p.vs1 + d0 * p.vs2, p.vs2, p.in_dtype, p.vec_ok, d0, p.D, fv);
+    const int64_t dst = dst0 + static_cast<int64_t>(h) * D + d0;
+    if (full_chunks) {
       *reinterpret_cast<uint4*>(static_cast<PoolT*>(p.kp) + dst) = Pack<PoolT>::pack(fk);
       *reinterpret_cast<uint4*>(static_cast<PoolT*>(p.vp) + dst) = Pack<PoolT>::pack(fv);
     } else {
-      for (int e = 0; e < NE && d0 + e < p.D; ++e) {
+      for (int e = 0; e < NE && d0 + e < D; ++e) {
         store_elem(p.kp, dst + e, p.pool_dtype, fk[e]);
         store_elem(p.vp, dst + e, p.pool_dtype, fv[e]);
       }
@@ -156,13 +163,14 @@ int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream) {
            ((st[0] * es) % 16) == 0 && ((st[1] * es) % 16) == 0 && (ne * es) % 16 == 0;
   };
   p.vec_ok = (a.kv_in_dtype != B200_DTYPE_F16) && aligned(a.k, a.k_stride) && aligned(a.v, a.v_stride);
-  const int64_t total = p.N * p.H * ((p.D + ne - 1) / ne);
-  int64_t blocks = (total + 255) / 256;
-  blocks = std::min<int64_t>(blocks, static_cast<int64_t>(dev.num_sms) * 16);
+  const int64_t chunks = p.H * ((p.D + ne - 1) / ne);
+  const int threads = chunks >= 256 ? 256 : static_cast<int>((chunks + 31) / 32 * 32);
+  if (p.N > 0x7fffffffLL) return fail(B200_ERR_UNSUPPORTED, "kv_scatter: too many tokens");
+  const unsigned blocks = static_cast<unsigned>(p.N);
   if (a.pool.dtype == B200_DTYPE_F32)
-    kv_scatter_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+    kv_scatter_kernel<float><<<blocks, threads, 0, stream>>>(p);
   else
-    kv_scatter_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+    kv_scatter_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kv_scatter launch");
   return B200_OK;
