@@ -8,10 +8,11 @@
 // tensor core: while one softmax group works on its scores, the MMAs of the
 // other group run.
 //
-// Warp roles (10 warps):
-//   warp 0   TMA producer: for each 128-key tile walks the block table and
-//            loads, per KV block, boxes {64 d, 1 head, rbox rows} of K and V
-//            with 128-byte swizzle into a 2-stage ring of this CTA.
+// Warp roles (11 warps):
+//   warps 0, 10  TMA producers of K and V: for each 128-key tile they walk
+//            the block table and load, per KV block, boxes {64 d, 1 head,
+//            rbox rows} with 128-byte swizzle into this CTA's K ring (3
+//            stages) and V ring (2 stages).
 //   warp 1   TMEM allocation (512 columns) and the MMA issuer (one thread):
 //              S_w  = Q_w K^T -> TMEM columns [128w, 128w+128)   (M=128,N=128)
 //              O_w += P_w V   -> TMEM columns [256+128w, +D)     (M=128,N=D)
@@ -43,7 +44,9 @@ namespace b200 {
 namespace {
 
 constexpr int kMaxSeqs = 128;  // sequences per launch (host splits larger batches)
-constexpr int kThreads = 320;  // producer, MMA, two 4-warp softmax groups
+constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
+constexpr int kKStages = 3;    // K ring depth (K is needed first, by the S MMAs)
+constexpr int kVStages = 2;    // V ring depth (V is needed after the softmax)
 constexpr int kBM = 128;       // queries per query tile (two tiles per CTA)
 constexpr int kBN = 128;       // keys per tile
 
@@ -202,9 +205,9 @@ struct Smem {
   static constexpr int HALVES = D / 64;            // 64-element (128-byte) column halves
   static constexpr int TILE = HALVES * 128 * 128;  // one 128-row operand tile
   static constexpr int Q0 = 0;                     // Q tiles 0 and 1
-  static constexpr int K0 = Q0 + 2 * TILE;         // K stage 0, K stage 1
-  static constexpr int V0 = K0 + 2 * TILE;         // V stage 0, V stage 1
-  static constexpr int BAR = V0 + 2 * TILE;
+  static constexpr int K0 = Q0 + 2 * TILE;         // K ring
+  static constexpr int V0 = K0 + kKStages * TILE;  // V ring
+  static constexpr int BAR = V0 + kVStages * TILE;
   static constexpr int BYTES = BAR + 256;
 };
 
@@ -277,19 +280,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   g.total = prefix + min(sd.T, g.i0 + 2 * kBM);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
-  uint64_t* kv_full = bars + 0;   // [2]
-  uint64_t* kv_empty = bars + 2;  // [2]
-  uint64_t* s_full = bars + 4;    // [2] per query tile
-  uint64_t* p_full = bars + 6;    // [2]
-  uint64_t* o_done = bars + 8;    // [2]
-  uint64_t* mma_idle = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 12);
+  uint64_t* k_full = bars + 0;    // [kKStages]
+  uint64_t* k_empty = bars + 3;   // [kKStages]
+  uint64_t* v_full = bars + 6;    // [kVStages]
+  uint64_t* v_empty = bars + 8;   // [kVStages]
+  uint64_t* s_full = bars + 10;   // [2] per query tile
+  uint64_t* p_full = bars + 12;   // [2]
+  uint64_t* o_done = bars + 14;   // [2]
+  uint64_t* mma_idle = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 18);
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 128);
       mbar_init(&o_done[s], 1);
@@ -308,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Q tiles: softmax group w loads query tile w; row r of a 128-row tile is
   // TMEM lane r, and a warp may only touch lanes [32*(warp%4), +32), so rows
   // follow (warp % 4, lane).
-  const int wg = warp >= 2 ? (warp - 2) >> 2 : -1;  // softmax group of this warp
+  const int wg = (warp >= 2 && warp < 10) ? (warp - 2) >> 2 : -1;  // softmax group
   const int r = (warp & 3) * 32 + lane;             // row within the group's tile
   if (wg >= 0)
     load_q_row<D>(smem + L::Q0 + wg * L::TILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
@@ -321,19 +332,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tmem_s = [&](int w) { return tmem + static_cast<uint32_t>(w * 128); };
   auto tmem_o = [&](int w) { return tmem + 256u + static_cast<uint32_t>(w * 128); };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    // Every lane issues TMA boxes: a K/V tile is (keys/rbox blocks) x (K, V)
-    // x (D/64 column halves) small boxes, and spreading their issue over the
-    // warp keeps the copy engine fed.
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------------------ producers
+    // Warp 0 streams K, warp 10 streams V, each through its own ring.  Every
+    // lane issues TMA boxes: a tile is (keys/rbox blocks) x (D/64 column
+    // halves) small boxes, and spreading their issue over the warp keeps the
+    // copy engine fed.
+    const bool is_k = warp == 0;
+    const int NS = is_k ? kKStages : kVStages;
+    uint64_t* full = is_k ? k_full : v_full;
+    uint64_t* empty = is_k ? k_empty : v_empty;
+    uint8_t* ring = smem + (is_k ? L::K0 : L::V0);
+    const CUtensorMap* map = is_k ? &tmk : &tmv;
     const int box_bytes = 64 * p.rbox * 2;
     const int boxes_per_tile = kBN / p.rbox;
-    constexpr int PER_BLOCK = 2 * L::HALVES;  // boxes per KV block (K/V x halves)
     int issued = 0;
     for (int j = 0; j < g.nmax; ++j) {
-      const int st = j & 1;
+      const int st = j % NS;
+      const uint32_t use = static_cast<uint32_t>(j / NS);
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(&empty[st], (use & 1u) ^ 1u) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || *reinterpret_cast<volatile int32_t*>(abort_flag)) {
         if (lane == 0 && !ok) {
@@ -346,14 +364,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
                                           (g.total - key0 + p.rbox - 1) >> p.rb_shift));
       if (lane == 0)
-        mbar_arrive_expect_tx(&kv_full[st], static_cast<uint32_t>(nb * PER_BLOCK * box_bytes));
+        mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * L::HALVES * box_bytes));
       __syncwarp();
-      uint8_t* kdst = smem + L::K0 + st * L::TILE;
-      uint8_t* vdst = smem + L::V0 + st * L::TILE;
-      for (int it = lane; it < nb * PER_BLOCK; it += 32) {
-        const int b = it / PER_BLOCK;
-        const int sel = it % PER_BLOCK;
-        const int half = sel % L::HALVES;
+      uint8_t* dst = ring + st * L::TILE;
+      for (int it = lane; it < nb * L::HALVES; it += 32) {
+        const int b = it / L::HALVES;
+        const int half = it % L::HALVES;
         const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
         const int64_t blk = key >> p.s_shift;
         int64_t phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
@@ -362,18 +378,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           phys = 0;
         }
         const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
-        const uint32_t off = half * 16384 + b * p.rbox * 128;
-        if (sel < L::HALVES)
-          tma_load_3d(kdst + off, &tmk, &kv_full[st], half * 64, h, row);
-        else
-          tma_load_3d(vdst + off, &tmv, &kv_full[st], half * 64, h, row);
+        tma_load_3d(dst + half * 16384 + b * p.rbox * 128, map, &full[st], half * 64, h, row);
       }
       ++issued;
     }
     if (lane == 0) {
-      const int first = issued > 2 ? issued - 2 : 0;
+      const int first = issued > NS ? issued - NS : 0;
       for (int j = first; j < issued; ++j)
-        if (!mbar_wait(&kv_full[j & 1], (j >> 1) & 1)) {
+        if (!mbar_wait(&full[j % NS], static_cast<uint32_t>(j / NS) & 1u)) {
           report(p.status, B200_DEV_WAIT_TIMEOUT);
           break;
         }
@@ -385,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
       bool ok = true;
       auto issue_s = [&](int w, int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
+        const int st = j % kKStages;
+        if (!mbar_wait(&k_full[st], static_cast<uint32_t>(j / kKStages) & 1u)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + L::Q0 + w * L::TILE);
         const uint32_t k_addr = smem_u32(smem + L::K0 + st * L::TILE);
@@ -397,19 +409,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                    smem_desc_sw128(k_addr + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[w]);
+        // The last S MMA of tile j releases its K stage.
+        if (w == (j < g.nkt[1] ? 1 : 0)) mma_commit(&k_empty[st]);
         return true;
       };
       for (int w = 0; ok && w < 2; ++w)
         if (g.nkt[w] > 0) ok = issue_s(w, 0);
       for (int j = 0; ok && j < g.nmax; ++j) {
-        const int st = j & 1;
-        const uint32_t v_addr = smem_u32(smem + L::V0 + st * L::TILE);
+        const int vst = j % kVStages;
+        const uint32_t v_addr = smem_u32(smem + L::V0 + vst * L::TILE);
+        bool v_ready = false;
         for (int w = 0; ok && w < 2; ++w) {
           if (j >= g.nkt[w]) continue;
           if (!mbar_wait(&p_full[w], j & 1)) {
             ok = false;
             break;
           }
+          if (!v_ready && !mbar_wait(&v_full[vst], static_cast<uint32_t>(j / kVStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          v_ready = true;
           tc_fence_after();
           // P (bf16 pairs over S_w's first 64 columns) is the TMEM A operand;
           // 16 keys per step = 8 columns.  MMAs of this thread execute in
@@ -423,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&o_done[w]);
           if (j + 1 < g.nkt[w] && !issue_s(w, j + 1)) ok = false;
         }
-        if (ok) mma_commit(&kv_empty[st]);
+        if (ok) mma_commit(&v_empty[vst]);  // the tile's last P.V releases its V stage
       }
       if (!ok) {
         report(p.status, B200_DEV_WAIT_TIMEOUT);
@@ -541,8 +561,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // may be unwritten); the group issuing the tile's first P.V does it.
       const int64_t valid = g.total - key0;
       const int first_w = j < g.nkt[0] ? 0 : 1;
+      if (w == first_w && valid < kBN) {
+        // V of this tile must have landed before its rows are cleared.
+        if (!mbar_wait(&v_full[j % kVStages], static_cast<uint32_t>(j / kVStages) & 1u)) {
+          ok = false;
+          break;
+        }
+      }
       if (w == first_w && valid < kBN && r >= valid) {
-        uint8_t* vrow = smem + L::V0 + (j & 1) * L::TILE + r * 128;
+        uint8_t* vrow = smem + L::V0 + (j % kVStages) * L::TILE + r * 128;
 #pragma unroll
         for (int half = 0; half < L::HALVES; ++half)
 #pragma unroll
