@@ -43,7 +43,7 @@
 namespace b200 {
 namespace {
 
-constexpr int kMaxSeqs = 128;  // sequences per launch (host splits larger batches)
+constexpr int kMaxSeqs = 64;   // sequences per launch (host splits larger batches)
 constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
 constexpr int kKStages = 3;    // K ring depth (K is needed first, by the S MMAs)
 constexpr int kVStages = 2;    // V ring depth (V is needed after the softmax)
@@ -64,10 +64,12 @@ struct SeqDesc {
 };
 
 struct PrefillParams {
+  CUtensorMap qmap[kMaxSeqs];  // per-sequence Q maps (valid when q_tma)
   int64_t P, S, H, D;
   int64_t layer;
   int32_t q_dtype, out_dtype, table_i64;
   int32_t q_vec, out_vec;  // 16-byte row access is legal for every sequence
+  int32_t q_tma;           // every sequence's q is bf16 and TMA-addressable
   int32_t rbox, rb_shift, s_shift;
   int32_t nseq;
   int32_t max_qtiles;
@@ -75,6 +77,8 @@ struct PrefillParams {
   float scale_log2;
   SeqDesc seq[kMaxSeqs];
 };
+// Kernel parameters (two K/V maps + this struct) stay under the 32764-byte limit.
+static_assert(sizeof(PrefillParams) + 2 * sizeof(CUtensorMap) <= 32764, "kernel parameters too large");
 
 // ------------------------------------------------------------ tcgen05 PTX
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -288,8 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = bars + 12;   // [2]
   uint64_t* o_done = bars + 14;   // [2]
   uint64_t* mma_idle = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 18);
+  uint64_t* q_full = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 19);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
@@ -306,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_done[s], 1);
     }
     mbar_init(mma_idle, 1);
+    mbar_init(q_full, p.q_tma ? 1 : 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -321,12 +327,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // follow (warp % 4, lane).
   const int wg = (warp >= 2 && warp < 10) ? (warp - 2) >> 2 : -1;  // softmax group
   const int r = (warp & 3) * 32 + lane;             // row within the group's tile
-  if (wg >= 0)
-    load_q_row<D>(smem + L::Q0 + wg * L::TILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
-  fence_proxy_async_shared();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Q tiles: by TMA from the K producer (zero-filled past T), else loaded
+  // here by the softmax threads; either way the MMA issuer waits on q_full,
+  // and K/V prefetch starts at once.
+  if (!p.q_tma && wg >= 0) {
+    load_q_row<D>(smem + L::Q0 + wg * L::TILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
+    fence_proxy_async_shared();
+    mbar_arrive(q_full);
+  }
   const uint32_t tmem = *tmem_slot;
   // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).
   auto tmem_s = [&](int w) { return tmem + static_cast<uint32_t>(w * 128); };
@@ -346,6 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const CUtensorMap* map = is_k ? &tmk : &tmv;
     const int box_bytes = 64 * p.rbox * 2;
     const int boxes_per_tile = kBN / p.rbox;
+    if (is_k && p.q_tma && lane == 0) {
+      const int ntiles = g.nkt[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(ntiles * L::HALVES * kBM * 128));
+      for (int w = 0; w < ntiles; ++w)
+        for (int half = 0; half < L::HALVES; ++half)
+          tma_load_3d(smem + L::Q0 + w * L::TILE + half * 16384, &p.qmap[seq], q_full, half * 64,
+                      h, g.i0 + w * kBM);
+    }
     int issued = 0;
     for (int j = 0; j < g.nmax; ++j) {
       const int st = j % NS;
@@ -389,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           report(p.status, B200_DEV_WAIT_TIMEOUT);
           break;
         }
+      if (is_k && p.q_tma && !mbar_wait(q_full, 0)) report(p.status, B200_DEV_WAIT_TIMEOUT);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -413,8 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w == (j < g.nkt[1] ? 1 : 0)) mma_commit(&k_empty[st]);
         return true;
       };
-      for (int w = 0; ok && w < 2; ++w)
-        if (g.nkt[w] > 0) ok = issue_s(w, 0);
+      // Stagger the two groups by half a period: group 1's first S is issued
+      // only once group 0 has produced its first P, so from then on one
+      // group's softmax overlaps the other group's MMAs instead of both
+      // groups contending for the exp unit while the tensor core idles.
+      ok = mbar_wait(q_full, 0);
+      if (ok && g.nkt[0] > 0) ok = issue_s(0, 0);
+      else if (ok && g.nkt[1] > 0) ok = issue_s(1, 0);
       for (int j = 0; ok && j < g.nmax; ++j) {
         const int vst = j % kVStages;
         const uint32_t v_addr = smem_u32(smem + L::V0 + vst * L::TILE);
@@ -422,6 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; ok && w < 2; ++w) {
           if (j >= g.nkt[w]) continue;
           if (!mbar_wait(&p_full[w], j & 1)) {
+            ok = false;
+            break;
+          }
+          if (j == 0 && w == 0 && g.nkt[1] > 0 && !issue_s(1, 0)) {
             ok = false;
             break;
           }
@@ -724,6 +753,30 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
       out_vec = out_vec && ov;
     }
     prm.max_qtiles = static_cast<int32_t>(max_qt);
+    // Q by TMA when every q is bf16 with unit innermost stride and 16-byte
+    // aligned rows/heads: dims {D, H, T}, box {64, 1, 128 rows}, swizzle 128B.
+    bool q_tma = a0.q_dtype == B200_DTYPE_BF16;
+    for (int64_t i = 0; i < cnt && q_tma; ++i) {
+      const b200_prefill_args_t& sq = seqs[base + i];
+      q_tma = sq.q_stride[2] == 1 && (reinterpret_cast<uintptr_t>(sq.q) % 16) == 0 &&
+              (sq.q_stride[0] * 2) % 16 == 0 && (sq.q_stride[1] * 2) % 16 == 0 &&
+              sq.q_stride[0] > 0 && sq.q_stride[1] > 0;
+    }
+    for (int64_t i = 0; i < cnt && q_tma; ++i) {
+      const b200_prefill_args_t& sq = seqs[base + i];
+      const uint64_t qd[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(sq.num_tokens)};
+      const uint64_t qs[2] = {static_cast<uint64_t>(sq.q_stride[1] * 2),
+                              static_cast<uint64_t>(sq.q_stride[0] * 2)};
+      const uint32_t qb[3] = {64u, 1u, static_cast<uint32_t>(kBM)};
+      if (encode_tensor_map(&prm.qmap[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                            const_cast<void*>(sq.q), qd, qs, qb,
+                            CU_TENSOR_MAP_SWIZZLE_128B) != B200_OK) {
+        q_tma = false;  // fall back to thread loads for this launch
+        clear_error();
+      }
+    }
+    prm.q_tma = q_tma ? 1 : 0;
     prm.q_vec = q_vec ? 1 : 0;
     prm.out_vec = out_vec ? 1 : 0;
     const dim3 grid(static_cast<unsigned>(max_qt * H), static_cast<unsigned>(cnt));

@@ -120,7 +120,10 @@ def test_prefill_bf16_kv_against_oracle(prefix, T, seed):
 @pytest.mark.parametrize("dim,bs,heads,prefix,T", [(64, 16, 4, 300, 130), (128, 8, 2, 40, 129),
                                                    (128, 32, 3, 1000, 64), (128, 256, 2, 600, 300),
                                                    (64, 64, 5, 0, 1), (128, 16, 1, 127, 1)])
-def test_prefill_tensor_core_shapes(dim, bs, heads, prefix, T):
+@pytest.mark.parametrize("q_kind", ["f32", "bf16_strided"])
+def test_prefill_tensor_core_shapes(dim, bs, heads, prefix, T, q_kind):
+    """fp32 q takes the thread-loaded Q path; bf16 q, here a strided view of a
+    fused [T, 3, H, D] projection, takes the TMA-loaded Q path."""
     from b200attn import chunked_prefill_b200, kv_scatter_b200
 
     c = cases.prefill_case(prefix, T, heads, dim, bs, 900 + dim + bs + T, dtype=torch.bfloat16,
@@ -129,14 +132,20 @@ def test_prefill_tensor_core_shapes(dim, bs, heads, prefix, T):
     pool = c.pool.to(d)
     status = torch.zeros(1, dtype=torch.int32, device=d)
     kv_scatter_b200(c.k.to(d), c.v.to(d), pool, c.slots, 1)
-    out = chunked_prefill_b200(c.q.float().to(d), pool, c.block_table, prefix, 1, status=status)
+    if q_kind == "f32":
+        q = c.q.float().to(d)
+    else:
+        fused = torch.zeros((T, 3, heads, dim), dtype=torch.bfloat16, device=d)
+        fused[:, 1] = c.q.to(d)
+        q = fused[:, 1]
+    out = chunked_prefill_b200(q, pool, c.block_table, prefix, 1, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     kp, vp = c.pool.k.clone(), c.pool.v.clone()
     oracle.kv_scatter(kp, vp, c.k, c.v, c.slots, 1)
     want = oracle.prefix_prefill_from_pool(c.q.float(), kp.float(), vp.float(), c.block_table,
                                            prefix, 1, compute_dtype=torch.float64).float()
-    err = (out.cpu() - want).abs().max().item()
+    err = (out.float().cpu() - want).abs().max().item()
     assert err <= 2e-2, f"max abs {err:.3e}"
 
 
