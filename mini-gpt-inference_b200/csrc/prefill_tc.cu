@@ -35,6 +35,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -44,6 +45,7 @@ namespace b200 {
 namespace {
 
 constexpr int kMaxSeqs = 64;   // sequences per launch (host splits larger batches)
+constexpr int kMaxWork = 2048; // (sequence, query pair) items per launch
 constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
 constexpr int kKStages = 3;    // K ring depth (K is needed first, by the S MMAs)
 constexpr int kVStages = 2;    // V ring depth (V is needed after the softmax)
@@ -76,6 +78,10 @@ struct PrefillParams {
   int32_t* status;
   float scale_log2;
   SeqDesc seq[kMaxSeqs];
+  // Work items, longest first: sequence | query pair << 8.  blockIdx.y picks
+  // one, blockIdx.x is the head, so the CTAs with the most key tiles start
+  // first and the short ones fill the tail of the launch.
+  uint32_t work[kMaxWork];
 };
 // Kernel parameters (two K/V maps + this struct) stay under the 32764-byte limit.
 static_assert(sizeof(PrefillParams) + 2 * sizeof(CUtensorMap) <= 32764, "kernel parameters too large");
@@ -266,9 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int seq = blockIdx.y;
-  const int h = blockIdx.x % static_cast<int>(p.H);
-  const int qp = blockIdx.x / static_cast<int>(p.H);
+  const uint32_t item = p.work[blockIdx.y];
+  const int seq = static_cast<int>(item & 0xFFu);
+  const int qp = static_cast<int>(item >> 8);
+  const int h = blockIdx.x;
   const SeqDesc& sd = p.seq[seq];
   Geom g;
   g.i0 = qp * 2 * kBM;
@@ -779,13 +786,34 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
     prm.q_tma = q_tma ? 1 : 0;
     prm.q_vec = q_vec ? 1 : 0;
     prm.out_vec = out_vec ? 1 : 0;
-    const dim3 grid(static_cast<unsigned>(max_qt * H), static_cast<unsigned>(cnt));
-    if (D == 128)
-      prefill_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
-    else
-      prefill_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "prefill_tc launch");
+    // Work list: every (sequence, query pair) with its key-tile count, sorted
+    // longest first (stable, so equal items keep sequence order).
+    std::vector<std::pair<int64_t, uint32_t>> items;
+    for (int64_t i = 0; i < cnt; ++i) {
+      const b200_prefill_args_t& s = seqs[base + i];
+      for (int64_t qp = 0; qp * 2 * kBM < s.num_tokens; ++qp) {
+        int64_t tiles = 0;
+        for (int w = 0; w < 2; ++w) {
+          const int64_t lo = qp * 2 * kBM + w * kBM;
+          if (lo < s.num_tokens)
+            tiles += ceil_div(s.prefix_len + std::min<int64_t>(s.num_tokens, lo + kBM), kBN);
+        }
+        items.emplace_back(tiles, static_cast<uint32_t>(i) | (static_cast<uint32_t>(qp) << 8));
+      }
+    }
+    std::stable_sort(items.begin(), items.end(),
+                     [](const auto& a, const auto& b) { return a.first > b.first; });
+    for (size_t w0 = 0; w0 < items.size(); w0 += kMaxWork) {
+      const size_t nw = std::min<size_t>(kMaxWork, items.size() - w0);
+      for (size_t k = 0; k < nw; ++k) prm.work[k] = items[w0 + k].second;
+      const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw));
+      if (D == 128)
+        prefill_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
+      else
+        prefill_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "prefill_tc launch");
+    }
   }
   return B200_OK;
 }
