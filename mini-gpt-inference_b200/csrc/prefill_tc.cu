@@ -12,8 +12,9 @@
 //   warps 0, 10  TMA producers of K and V: for each 128-key tile they walk
 //            the block table and load, per KV block, boxes {64 d, 1 head,
 //            rbox rows} with 128-byte swizzle into this CTA's K ring (3
-//            stages) and V ring (2 stages).
-//   warp 1   TMEM allocation (512 columns) and the MMA issuer (one thread):
+//            stages) and V ring (2 stages); warp 0 also loads the Q tiles.
+//   warp 1   TMEM allocation (512 columns) and the MMA issuer (whole warp,
+//            one elected lane issues):
 //              S_w  = Q_w K^T -> TMEM columns [128w, 128w+128)   (M=128,N=128)
 //              O_w += P_w V   -> TMEM columns [256+128w, +D)     (M=128,N=D)
 //            Q, K and P are K-major SW128 operands; V is read MN-major.
@@ -49,6 +50,9 @@ constexpr int kMaxWork = 2048; // (sequence, query pair) items per launch
 constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
 constexpr int kKStages = 3;    // K ring depth (K is needed first, by the S MMAs)
 constexpr int kVStages = 2;    // V ring depth (V is needed after the softmax)
+// Every kPolyEvery-th exponential pair of P runs on the FMA pipes (0: all on
+// MUFU; measured fastest while MUFU is not the limiting unit).
+constexpr int kPolyEvery = 0;
 constexpr int kBM = 128;       // queries per query tile (two tiles per CTA)
 constexpr int kBN = 128;       // keys per tile
 
@@ -103,12 +107,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major)
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// The MMA helpers are called by a whole converged warp with warp-uniform
+// operands; elect.sync picks one lane (the lowest, lane 0, every time) to
+// issue, so the commits track the MMAs of the same thread.
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -117,17 +125,21 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b
 __device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
       "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -198,6 +210,38 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Base-2 exponential of a pair on the FMA pipes, so that part of the softmax
+// exponentials bypass the 16/clock/SM MUFU unit.  x is clamped to >= -125
+// (the result stays a normal float; the true value is below 2^-125 and
+// vanishes in the row sum and in bf16 P anyway).  Range reduction: adding
+// 1.5 * 2^23 rounds x to the nearest integer j (left in the low mantissa
+// bits of t) and leaves f = x - j in [-0.5, 0.5]; 2^f is a degree-3
+// polynomial fitted to 2^f on [-0.5, 0.5] by weighted least squares with
+// Lawson reweighting toward minimax (max relative error 7.5e-5, below the
+// 2^-8 rounding of bf16 P; exp2_poly_fit.py regenerates the coefficients);
+// j is added to the exponent field of the polynomial's bit pattern.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 one2 = make_float2(1.f, 1.f), mone2 = make_float2(-1.f, -1.f);
+  const float2 t = ffma2(x, one2, make_float2(12582912.f, 12582912.f));
+  const float2 jf = ffma2(t, one2, make_float2(-12582912.f, -12582912.f));
+  const float2 f = ffma2(jf, mone2, x);
+  float2 q = ffma2(make_float2(0.0551716648f, 0.0551716648f), f,
+                   make_float2(0.2426111251f, 0.2426111251f));
+  q = ffma2(q, f, make_float2(0.6932609677f, 0.6932609677f));
+  q = ffma2(q, f, make_float2(0.9999280572f, 0.9999280572f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// max(a, b, c) in one instruction (three-input max, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -207,6 +251,51 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // tile of 128-byte rows.
 __device__ __forceinline__ uint32_t sw128(int r, int ch) {
   return static_cast<uint32_t>(r) * 128u + (static_cast<uint32_t>(ch ^ (r & 7)) << 4);
+}
+
+// Pass 2 of the softmax for this thread's S row (128 columns in TMEM at
+// `srow`): p = 2^(s * scale - m) for keys c <= lim (all keys when !MASK),
+// written as bf16 pairs over the S columns already read (chunk [c, c+32) ->
+// P columns [c/2, c/2 + 16)).  The next 32-column chunk is loaded while the
+// current one is computed.  Returns the row sum of p.
+template <bool MASK>
+__device__ __forceinline__ float p_pass(uint32_t srow, float scale, float neg_m, int lim) {
+  const float2 sc2 = make_float2(scale, scale);
+  const float2 nm2 = make_float2(neg_m, neg_m);
+  const float2 one2 = make_float2(1.f, 1.f);
+  float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                  make_float2(0.f, 0.f)};
+  float sv[2][32];
+  tmem_ld32(srow, sv[0]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < kBN; c += 32) {
+    const int cur = (c >> 5) & 1;
+    if (c + 32 < kBN) tmem_ld32(srow + c + 32, sv[cur ^ 1]);
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const float2 a = ffma2(make_float2(sv[cur][e], sv[cur][e + 1]), sc2, nm2);
+      float p0, p1;
+      if (kPolyEvery > 0 && (e >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) {
+        const float2 pp = ex2_poly2(a);  // this pair on the FMA pipes
+        p0 = pp.x;
+        p1 = pp.y;
+      } else {
+        p0 = ex2_approx(a.x);
+        p1 = ex2_approx(a.y);
+      }
+      if (MASK) {
+        p0 = c + e <= lim ? p0 : 0.f;
+        p1 = c + e + 1 <= lim ? p1 : 0.f;
+      }
+      rs[(e >> 1) & 3] = ffma2(make_float2(p0, p1), one2, rs[(e >> 1) & 3]);
+      pk[e >> 1] = pack_bf16(p0, p1);
+    }
+    tmem_st16(srow + (c >> 1), pk);
+    if (c + 32 < kBN) tmem_wait_ld();
+  }
+  return ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
 }
 
 // Shared-memory layout (offsets from a 1024-aligned base).
@@ -291,17 +380,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   g.total = prefix + min(sd.T, g.i0 + 2 * kBM);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
-  uint64_t* k_full = bars + 0;    // [kKStages]
-  uint64_t* k_empty = bars + 3;   // [kKStages]
-  uint64_t* v_full = bars + 6;    // [kVStages]
-  uint64_t* v_empty = bars + 8;   // [kVStages]
-  uint64_t* s_full = bars + 10;   // [2] per query tile
-  uint64_t* p_full = bars + 12;   // [2]
-  uint64_t* o_done = bars + 14;   // [2]
-  uint64_t* mma_idle = bars + 16;
-  uint64_t* q_full = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  int32_t* abort_flag = reinterpret_cast<int32_t*>(bars + 19);
+  uint64_t* k_full = bars;                      // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;        // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;        // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;        // [kVStages]
+  uint64_t* s_full = v_empty + kVStages;        // [2] per query tile
+  uint64_t* p_full = s_full + 2;                // [2]
+  uint64_t* o_done = p_full + 2;                // [2]
+  uint64_t* mma_idle = o_done + 2;
+  uint64_t* q_full = mma_idle + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(q_full + 2);
+  static_assert((2 * kKStages + 2 * kVStages + 10) * 8 <= 256, "barrier area too small");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
@@ -372,10 +462,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(smem + L::Q0 + w * L::TILE + half * 16384, &p.qmap[seq], q_full, half * 64,
                       h, g.i0 + w * kBM);
     }
+    // A tile has at most 32 boxes (rbox >= 8, two column halves), so each
+    // lane issues at most one: lane -> (block b, half).
+    const int b = lane / L::HALVES;
+    const int half = lane % L::HALVES;
     int issued = 0;
     for (int j = 0; j < g.nmax; ++j) {
       const int st = j % NS;
       const uint32_t use = static_cast<uint32_t>(j / NS);
+      const int64_t key0 = static_cast<int64_t>(j) * kBN;
+      const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
+                                          (g.total - key0 + p.rbox - 1) >> p.rb_shift));
+      // The block-table read does not depend on the ring slot: start it
+      // before waiting for the slot so its latency overlaps the wait.
+      const bool mine = lane < nb * L::HALVES;
+      const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
+      const int64_t blk = key >> p.s_shift;
+      int64_t phys = 0;
+      if (mine) {
+        phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
+        if (phys < 0 || phys >= p.P) {
+          report(p.status, B200_DEV_BAD_BLOCK);
+          phys = 0;
+        }
+      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&empty[st], (use & 1u) ^ 1u) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -386,23 +496,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         break;
       }
-      const int64_t key0 = static_cast<int64_t>(j) * kBN;
-      const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
-                                          (g.total - key0 + p.rbox - 1) >> p.rb_shift));
       if (lane == 0)
         mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * L::HALVES * box_bytes));
       __syncwarp();
-      uint8_t* dst = ring + st * L::TILE;
-      for (int it = lane; it < nb * L::HALVES; it += 32) {
-        const int b = it / L::HALVES;
-        const int half = it % L::HALVES;
-        const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
-        const int64_t blk = key >> p.s_shift;
-        int64_t phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
-        if (phys < 0 || phys >= p.P) {
-          report(p.status, B200_DEV_BAD_BLOCK);
-          phys = 0;
-        }
+      if (mine) {
+        uint8_t* dst = ring + st * L::TILE;
         const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
         tma_load_3d(dst + half * 16384 + b * p.rbox * 128, map, &full[st], half * 64, h, row);
       }
@@ -419,21 +517,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (values stay warp-uniform); every
+    // lane waits on the barriers itself and a vote makes the outcome uniform.
+    {
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+      };
       constexpr uint32_t idesc_s = idesc_bf16(128, 128, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
       bool ok = true;
+      // Descriptors of the tile bases; a step's descriptor adds its byte
+      // offset / 16 to the 14-bit address field (no carry: smem < 256 KB).
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::Q0), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::K0), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), 16384, 1024);
+      constexpr uint64_t kTileUnits = L::TILE >> 4;
       auto issue_s = [&](int w, int j) -> bool {
         const int st = j % kKStages;
-        if (!mbar_wait(&k_full[st], static_cast<uint32_t>(j / kKStages) & 1u)) return false;
+        if (!wait_all(&k_full[st], static_cast<uint32_t>(j / kKStages) & 1u)) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + L::Q0 + w * L::TILE);
-        const uint32_t k_addr = smem_u32(smem + L::K0 + st * L::TILE);
+        const uint64_t dq = dq0 + static_cast<uint64_t>(w) * kTileUnits;
+        const uint64_t dk = dk0 + static_cast<uint64_t>(st) * kTileUnits;
+        const uint32_t ts = tmem_s(w);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16(tmem_s(w), smem_desc_sw128(q_addr + koff, 16, 1024),
-                   smem_desc_sw128(k_addr + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          mma_bf16(ts, dq + koff, dk + koff, idesc_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[w]);
         // The last S MMA of tile j releases its K stage.
@@ -444,16 +553,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // only once group 0 has produced its first P, so from then on one
       // group's softmax overlaps the other group's MMAs instead of both
       // groups contending for the exp unit while the tensor core idles.
-      ok = mbar_wait(q_full, 0);
+      ok = wait_all(q_full, 0);
       if (ok && g.nkt[0] > 0) ok = issue_s(0, 0);
       else if (ok && g.nkt[1] > 0) ok = issue_s(1, 0);
       for (int j = 0; ok && j < g.nmax; ++j) {
         const int vst = j % kVStages;
-        const uint32_t v_addr = smem_u32(smem + L::V0 + vst * L::TILE);
+        const uint64_t dv = dv0 + static_cast<uint64_t>(vst) * kTileUnits;
+        const int w_last = j < g.nkt[1] ? 1 : 0;  // the last group that has tile j
         bool v_ready = false;
         for (int w = 0; ok && w < 2; ++w) {
           if (j >= g.nkt[w]) continue;
-          if (!mbar_wait(&p_full[w], j & 1)) {
+          if (!wait_all(&p_full[w], j & 1)) {
             ok = false;
             break;
           }
@@ -461,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (!v_ready && !mbar_wait(&v_full[vst], static_cast<uint32_t>(j / kVStages) & 1u)) {
+          if (!v_ready && !wait_all(&v_full[vst], static_cast<uint32_t>(j / kVStages) & 1u)) {
             ok = false;
             break;
           }
@@ -471,23 +581,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 16 keys per step = 8 columns.  MMAs of this thread execute in
           // issue order, so S_w of the next tile is written only after this
           // P.V has read P.
+          const uint32_t to = tmem_o(w), ts = tmem_s(w);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_bf16_ts(tmem_o(w), tmem_s(w) + kk * 8,
-                        smem_desc_sw128(v_addr + kk * 2048, 16384, 1024), idesc_o,
+            mma_bf16_ts(to, ts + kk * 8, dv + static_cast<uint64_t>(kk * 128), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&o_done[w]);
+          // The tile's last P.V releases its V stage (before the next S is
+          // issued, so the release does not wait for that S as well).
+          if (w == w_last) mma_commit(&v_empty[vst]);
           if (j + 1 < g.nkt[w] && !issue_s(w, j + 1)) ok = false;
         }
-        if (ok) mma_commit(&v_empty[vst]);  // the tile's last P.V releases its V stage
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         report(p.status, B200_DEV_WAIT_TIMEOUT);
         *abort_flag = 1;
       }
-      // Wait until every MMA this thread issued has completed.
+      // Wait until every MMA the warp issued has completed.
       mma_commit(mma_idle);
-      if (!mbar_wait(mma_idle, 0)) report(p.status, B200_DEV_WAIT_TIMEOUT);
+      if (!wait_all(mma_idle, 0) && lane == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
     }
     __syncwarp();
   } else {
@@ -519,19 +631,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp_live) {
         // Pass 1: row max of the masked raw scores (the scale is positive, so
         // it is applied once to the max).
-        float mx = -INFINITY;
+        float mx;
         {
           float sv[kBN];  // one TMEM round trip for the whole row
 #pragma unroll
           for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s(w) + lane_base + c, sv + c);
           tmem_wait_ld();
-          if (!need_mask) {
+          // Eight independent chains of three-input max, then a tree.
+          float mp[8];
+          if (need_mask) {
 #pragma unroll
-            for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, sv[e]);
+            for (int a = 0; a < 8; ++a)
+              mp[a] = fmaxf(2 * a <= lim ? sv[2 * a] : -INFINITY,
+                            2 * a + 1 <= lim ? sv[2 * a + 1] : -INFINITY);
+#pragma unroll
+            for (int e = 16; e < kBN; e += 16)
+#pragma unroll
+              for (int a = 0; a < 8; ++a)
+                mp[a] = fmax3(mp[a], e + 2 * a <= lim ? sv[e + 2 * a] : -INFINITY,
+                              e + 2 * a + 1 <= lim ? sv[e + 2 * a + 1] : -INFINITY);
           } else {
 #pragma unroll
-            for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, e <= lim ? sv[e] : -INFINITY);
+            for (int a = 0; a < 8; ++a) mp[a] = fmaxf(sv[2 * a], sv[2 * a + 1]);
+#pragma unroll
+            for (int e = 16; e < kBN; e += 16)
+#pragma unroll
+              for (int a = 0; a < 8; ++a) mp[a] = fmax3(mp[a], sv[e + 2 * a], sv[e + 2 * a + 1]);
           }
+          mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
         }
         mx *= p.scale_log2;
         // Lazy rescale: keep the old max unless the new one exceeds it by
@@ -540,8 +667,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         rescale = __any_sync(0xffffffffu, m_use != m) && j > 0;
         alpha = ex2_approx(m - m_use);
       }
+      if (warp_live) {
+        // Pass 2: probabilities, written back as bf16 pairs over the S
+        // columns already consumed; the masked variant is a separate
+        // instantiation so unmasked tiles carry no per-element selects.
+        const float rsum = need_mask ? p_pass<true>(tmem_s(w) + lane_base, p.scale_log2, -m_use, lim)
+                                     : p_pass<false>(tmem_s(w) + lane_base, p.scale_log2, -m_use, lim);
+        l = l * alpha + rsum;
+        m = m_use;
+      }
       if (j > 0) {
-        // O is stable once the previous P.V completed.
+        // O is stable once the previous P.V completed (already the case once
+        // S of this tile is complete: the MMAs complete in issue order).  The
+        // rescale runs after pass 2, before this tile's P.V is issued.
         if (!mbar_wait(&o_done[w], (j - 1) & 1)) {
           ok = false;
           break;
@@ -558,39 +696,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(tmem_o(w) + lane_base + c, o);
           }
         }
-      }
-      if (warp_live) {
-        // Pass 2: probabilities (packed FMA for the exponent argument and the
-        // row sum), bf16 pairs written over the S columns already consumed
-        // (chunk c -> P columns [c/2, c/2 + 16)).
-        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-        const float2 nm2 = make_float2(-m_use, -m_use);
-        const float2 one2 = make_float2(1.f, 1.f);
-        float2 rs2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < kBN; c += 64) {
-          float sv[64];  // two chunks per TMEM round trip
-          tmem_ld32(tmem_s(w) + lane_base + c, sv);
-          tmem_ld32(tmem_s(w) + lane_base + c + 32, sv + 32);
-          tmem_wait_ld();
-          uint32_t pk[32];
-#pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            const float2 a = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nm2);
-            float p0 = ex2_approx(a.x), p1 = ex2_approx(a.y);
-            if (need_mask) {
-              p0 = c + e <= lim ? p0 : 0.f;
-              p1 = c + e + 1 <= lim ? p1 : 0.f;
-            }
-            rs2 = ffma2(make_float2(p0, p1), one2, rs2);
-            pk[e >> 1] = pack_bf16(p0, p1);
-          }
-          // Chunk [c, c+64) -> P columns [c/2, c/2 + 32): all already read.
-          tmem_st16(tmem_s(w) + lane_base + (c >> 1), pk);
-          tmem_st16(tmem_s(w) + lane_base + (c >> 1) + 16, pk + 16);
-        }
-        l = l * alpha + (rs2.x + rs2.y);
-        m = m_use;
       }
       tmem_wait_st();
       // Zero V rows past the last valid key of the last tile (pool rows there
