@@ -19,6 +19,12 @@ class BlockManager:
         self.block_size = block_size
         self.free_blocks = list(range(num_blocks - 1, -1, -1))
         self.block_owner: dict[int, str] = {}
+        self._free_listeners: list = []
+
+    def add_free_listener(self, fn) -> None:
+        """fn(seq) runs after free() returns a sequence's blocks (finish or
+        preemption), e.g. to drop device-side copies of its block table."""
+        self._free_listeners.append(fn)
 
     def _take_block(self, seq: SequenceState) -> int:
         if not self.free_blocks:
@@ -65,6 +71,8 @@ class BlockManager:
             self.free_blocks.append(blk)
         seq.block_table.clear()
         seq.length = 0
+        for fn in self._free_listeners:
+            fn(seq)
         return released
 
     def check_invariants(self, sequences: list[SequenceState]) -> None:

@@ -6,13 +6,17 @@ input tokens (:68-120); a decode step reserves one append slot per request,
 builds DecodeBatchMetadata with context length = length + 1 and -1-padded
 block tables (:123-216), and samples greedily with argmax (:272-304).
 The device copies of a step's metadata are made once per step and shared by
-every layer.
+every layer.  With device_tables the step's metadata comes from
+DeviceDecodeState (persistent device block tables, one packed upload per
+step); with graphs the decode step is also replayed from a CUDA graph.
 """
 from __future__ import annotations
 
 import torch
 
 from .block_manager import BlockManager
+from .decode_graphs import DecodeGraphs
+from .decode_state import DeviceDecodeState
 from .kv_pool import DecodeBatchMetadata, KVBlockPool
 from .model import MiniGPT
 from .sequence import SequenceState
@@ -26,8 +30,16 @@ def _to_device(values, device) -> torch.Tensor:
 
 
 class ModelRunner:
-    def __init__(self, model: MiniGPT, kv_pool: KVBlockPool, block_manager: BlockManager):
+    def __init__(self, model: MiniGPT, kv_pool: KVBlockPool, block_manager: BlockManager, *,
+                 device_tables: bool = False, graphs: bool = False, max_rows: int = 0,
+                 max_blocks: int = 0, scratch_block: int = -1):
         self.model, self.kv_pool, self.block_manager = model, kv_pool, block_manager
+        self.state = None
+        self.graphs = None
+        if device_tables or graphs:
+            self.state = DeviceDecodeState(block_manager, max_rows, max_blocks, kv_pool.k.device)
+        if graphs:
+            self.graphs = DecodeGraphs(model, kv_pool, self.state, scratch_block)
 
     @property
     def device(self) -> torch.device:
@@ -61,9 +73,19 @@ class ModelRunner:
         return input_ids, meta
 
     def decode_batch(self, sequences: list[SequenceState]):
+        """(last-position logits or None, greedy token ids) of one decode step."""
         if not sequences:
             return []
-        input_ids, meta = self.prepare_decode_batch(sequences)
+        if self.state is not None:
+            slots = [self.block_manager.reserve_append_slot(s)[2] for s in sequences]
+            input_ids, meta, rows = self.state.build(sequences, slots)
+            if self.graphs is not None and len(sequences) <= self.graphs.max_batch():
+                tokens = self.graphs.run(input_ids, meta, rows).tolist()
+                for s in sequences:
+                    s.length += 1
+                return None, tokens
+        else:
+            input_ids, meta = self.prepare_decode_batch(sequences)
         logits = self.model.decode_batch(input_ids, meta, self.kv_pool)
         for s in sequences:
             s.length += 1

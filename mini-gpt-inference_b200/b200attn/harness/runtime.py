@@ -181,12 +181,23 @@ class MiniRuntime:
 
 def build_runtime(model: MiniGPT, *, num_blocks: int, block_size: int, max_running: int,
                   token_budget: int, policy: str, n_head: int, head_dim: int,
-                  kv_dtype: torch.dtype = torch.float32) -> MiniRuntime:
-    """A runtime over a fresh (uninitialised) KV pool on the model's device."""
+                  kv_dtype: torch.dtype = torch.float32, device_tables: bool = False,
+                  graphs: bool = False) -> MiniRuntime:
+    """A runtime over a fresh (uninitialised) KV pool on the model's device.
+
+    device_tables: decode metadata from persistent device block tables.
+    graphs: also replay the decode step from CUDA graphs (implies
+    device_tables); the pool then holds one extra block past the block
+    manager's range, the padding rows' scratch block.
+    """
     device = next(model.parameters()).device
     bm = BlockManager(num_blocks, block_size)
-    pool = KVBlockPool(model.n_layer, num_blocks, block_size, n_head, head_dim, device=device,
+    pool_blocks = num_blocks + (1 if graphs else 0)
+    pool = KVBlockPool(model.n_layer, pool_blocks, block_size, n_head, head_dim, device=device,
                        dtype=kv_dtype)
     sch = Scheduler(bm, max_running=max_running, max_num_batched_tokens=token_budget,
                     preemption_policy=policy)
-    return MiniRuntime(ModelRunner(model, pool, bm), sch)
+    max_blocks = -(-model.block_size // block_size)  # positions bound the sequence length
+    runner = ModelRunner(model, pool, bm, device_tables=device_tables, graphs=graphs,
+                         max_rows=max_running, max_blocks=max_blocks, scratch_block=num_blocks)
+    return MiniRuntime(runner, sch)

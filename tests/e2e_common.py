@@ -15,8 +15,13 @@ def prompts() -> list[list[int]]:
     return [torch.randint(0, CFG2["vocab"], (p,), generator=g).tolist() for p in CFG2["prompts"]]
 
 
-def run_cfg2(run_name: str, device: str, backend=None):
-    """Runs configuration 2 through the harness; returns (tokens, counts, runtime)."""
+def run_cfg2(run_name: str, device: str, backend=None, mode: str = "eager"):
+    """Runs configuration 2 through the harness; returns (tokens, counts, runtime).
+
+    mode: "eager" (host-built metadata per step), "device_tables" (persistent
+    device block tables) or "graphs" (device tables + CUDA-graph decode)."""
+    if mode not in ("eager", "device_tables", "graphs"):
+        raise ValueError(mode)
     from b200attn.harness import MiniGPT, SequenceState, build_runtime, init_weights
 
     model = MiniGPT(n_embd=CFG2["n_embd"], n_head=CFG2["n_head"], vocab_size=CFG2["vocab"],
@@ -27,7 +32,8 @@ def run_cfg2(run_name: str, device: str, backend=None):
     rt = build_runtime(model, num_blocks=run["num_blocks"], block_size=CFG2["block_size"],
                        max_running=CFG2["max_running"], token_budget=CFG2["token_budget"],
                        policy=run["policy"], n_head=CFG2["n_head"],
-                       head_dim=CFG2["n_embd"] // CFG2["n_head"])
+                       head_dim=CFG2["n_embd"] // CFG2["n_head"],
+                       device_tables=mode != "eager", graphs=mode == "graphs")
     rt.runner.kv_pool.k.fill_(float("nan"))  # unwritten KV must never be read
     rt.runner.kv_pool.v.fill_(float("nan"))
     reqs = [SequenceState(seq_id=f"r{i}", prompt_tokens=p, max_tokens=len(p) + CFG2["output_len"])

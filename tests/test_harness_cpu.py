@@ -12,15 +12,51 @@ from e2e_common import GOLDEN, run_cfg2
 from oracle_backend import OracleBackend
 
 
+@pytest.mark.parametrize("mode", ["eager", "device_tables"])
 @pytest.mark.parametrize("run_name", ["ample", "capped"])
-def test_cfg2_tokens_and_counts_match_reference(run_name):
+def test_cfg2_tokens_and_counts_match_reference(run_name, mode):
     torch.set_num_threads(4)
-    tokens, counts, _ = run_cfg2(run_name, "cpu", backend=OracleBackend())
+    tokens, counts, rt = run_cfg2(run_name, "cpu", backend=OracleBackend(), mode=mode)
     want = GOLDEN[f"{run_name}/sdpa_v2"]
     assert tokens == want["tokens"]
     assert counts == want["counts"]
     if run_name == "capped":
         assert counts["preemptions"] > 0 and counts["repeated_kv_tokens"] > 0
+    if mode == "device_tables":
+        assert not rt.runner.state.row_of  # every finished request gave its row back
+
+
+def test_device_decode_state_matches_host_metadata(monkeypatch):
+    """Step by step, the device tables give the metadata minivllm's host
+    builder would (model_runner.py:123-216: positions, length + 1, the
+    sequence's blocks, the append slot), and entries are uploaded once per
+    block (again only after a preemption freed them)."""
+    from b200attn.harness.decode_state import DeviceDecodeState
+
+    checked = {"steps": 0, "full_resend": 0}
+    orig = DeviceDecodeState.build
+    bs = GOLDEN["config"]["block_size"]
+
+    def build(self, sequences, slots):
+        ids, meta, rows = orig(self, sequences, slots)
+        assert ids[:, 0].tolist() == [s.last_token for s in sequences]
+        assert meta.positions.tolist() == [s.length for s in sequences]
+        assert meta.context_lengths.tolist() == [s.length + 1 for s in sequences]
+        assert meta.slot_mapping.tolist() == slots
+        for s, row in zip(sequences, meta.block_tables.tolist()):
+            n = -(-(s.length + 1) // bs)
+            assert row[:n] == s.block_table[:n]
+        checked["steps"] += 1
+        checked["full_resend"] += sum(len(s.block_table) for s in sequences)
+        return ids, meta, rows
+
+    monkeypatch.setattr(DeviceDecodeState, "build", build)
+    torch.set_num_threads(4)
+    tokens, counts, rt = run_cfg2("capped", "cpu", backend=OracleBackend(), mode="device_tables")
+    assert tokens == GOLDEN["capped/sdpa_v2"]["tokens"]
+    assert counts["preemptions"] > 0 and checked["steps"] > 0
+    # Each block crosses once per residency instead of once per step.
+    assert 0 < rt.runner.state.uploaded_entries * 4 < checked["full_resend"]
 
 
 class FakeRunner:
@@ -92,3 +128,12 @@ def test_harness_rejects_requests_like_the_reference():
         sch.add_request(SequenceState(seq_id="c", prompt_tokens=[1] * 8, max_tokens=20))
     with pytest.raises(ValueError):
         Scheduler(BlockManager(2, 4), 1, 8, preemption_policy="lru")
+
+
+def test_graph_buckets_cover_every_batch():
+    from b200attn.harness.decode_graphs import bucket_sizes
+
+    for rows in (1, 4, 8, 9, 64, 100, 256):
+        sizes = bucket_sizes(rows)
+        assert sizes == sorted(set(sizes)) and sizes[-1] == rows
+        assert all(any(n >= b for n in sizes) for b in range(1, rows + 1))
