@@ -298,13 +298,22 @@ def make_workload(name, rank, device, args):
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """Samples SM clocks and clock-event (throttle) reasons of the GPUs in use
-    every few milliseconds while the timed region runs (NVML, read-only)."""
+    every few milliseconds (NVML, read-only).  The sampler starts before the
+    warm-up so that it is running when the timed region begins; summary()
+    keeps the samples taken between mark_start() and mark_stop()."""
 
     def __init__(self, indices: list, period_s: float = 0.002):
         self.indices, self.period = indices, period_s
-        self.samples: list[tuple[float, float, int]] = []
+        self.samples: list[tuple[float, float, float, int]] = []  # (t, sm, max, reasons)
         self._stop = None
         self._thread = None
+        self._t0, self._t1 = None, None
+
+    def mark_start(self) -> None:
+        self._t0 = time.perf_counter()
+
+    def mark_stop(self) -> None:
+        self._t1 = time.perf_counter()
 
     def _run(self):
         import pynvml
@@ -320,7 +329,7 @@ class ClockSampler:
                     sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
                     mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
                     rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    self.samples.append((float(sm), float(mx), int(rs)))
+                    self.samples.append((time.perf_counter(), float(sm), float(mx), int(rs)))
                 self._stop.wait(self.period)
         except Exception:
             pass
@@ -344,17 +353,20 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
-        if not self.samples:
+        t0 = self._t0 if self._t0 is not None else float("-inf")
+        t1 = self._t1 if self._t1 is not None else float("inf")
+        window = [s[1:] for s in self.samples if t0 <= s[0] <= t1]
+        if not window:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         import pynvml
         names = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
                  "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
                  "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
                  "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
-        reasons = sorted(n for n, bit in names.items() if any(s[2] & bit for s in self.samples))
-        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
-                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
-                "samples": len(self.samples), "source": "nvml"}
+        reasons = sorted(n for n, bit in names.items() if any(s[2] & bit for s in window))
+        return {"sm_mhz": statistics.median(s[0] for s in window),
+                "sm_max_mhz": max(s[1] for s in window), "reasons": reasons,
+                "samples": len(window), "source": "nvml"}
 
 
 def gpu_indices(world: int) -> list:
@@ -476,7 +488,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     wl = make_workload(args.workload, rank, dev, args)
     stream = torch.cuda.current_stream(dev)
-    with torch.inference_mode():
+    with torch.inference_mode(), ClockSampler(gpu_indices(world)) as clocks:
         wl.prepare()
         for _ in range(args.warmup):
             wl.step()
@@ -485,12 +497,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             dist.barrier()
         torch.cuda.synchronize(dev)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(gpu_indices(world)) as clocks:
-            ev0.record(stream)
-            for _ in range(args.steps):
-                wl.step()
-            ev1.record(stream)
-            torch.cuda.synchronize(dev)
+        clocks.mark_start()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            wl.step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        clocks.mark_stop()
         ms = ev0.elapsed_time(ev1)
         if pg:
             dist.barrier()
