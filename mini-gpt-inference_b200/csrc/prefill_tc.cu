@@ -203,6 +203,16 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Two consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, uint32_t a, uint32_t b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(a), "r"(b)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t& a, uint32_t& b) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(taddr)
+               : "memory");
+}
+
 // Hardware base-2 exponential (MUFU), flushing denormal results to zero.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -347,8 +357,17 @@ __device__ __forceinline__ void load_q_row(uint8_t* tile, int r, int i, int h, c
 struct Geom {
   int i0;          // first query of the CTA
   int nkt[2];      // key tiles of query tile 0 / 1 (0 = tile inactive)
-  int nmax;        // max(nkt)
+  int nmax;        // max(nkt): key tiles streamed through the rings
   int64_t total;   // keys any query of the CTA may see
+  // Key split: with one query tile (and >= 2 key tiles) both softmax groups
+  // work on it, group w taking key tiles w, w+2, w+4, ... with its own O,
+  // max and sum; group 0 merges the two at the end.
+  bool split;
+  int cnt[2];      // key tiles group w processes
+  __device__ int tile(int w, int k) const { return split ? 2 * k + w : k; }
+  __device__ int qtile(int w) const { return split ? 0 : w; }
+  // The last group whose S or P.V reads key tile j (releases its stages).
+  __device__ int last_user(int j) const { return split ? (j & 1) : (j < nkt[1] ? 1 : 0); }
 };
 
 template <int D>
@@ -378,6 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   g.nmax = max(g.nkt[0], g.nkt[1]);
   g.total = prefix + min(sd.T, g.i0 + 2 * kBM);
+  g.split = g.nkt[1] == 0 && g.nkt[0] >= 2;
+  g.cnt[0] = g.split ? (g.nkt[0] + 1) / 2 : g.nkt[0];
+  g.cnt[1] = g.split ? g.nkt[0] / 2 : g.nkt[1];
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* k_full = bars;                      // [kKStages]
@@ -532,11 +554,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::K0), 16, 1024);
       const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), 16384, 1024);
       constexpr uint64_t kTileUnits = L::TILE >> 4;
-      auto issue_s = [&](int w, int j) -> bool {
+      // S of group w's k-th key tile.
+      auto issue_s = [&](int w, int k) -> bool {
+        const int j = g.tile(w, k);
         const int st = j % kKStages;
         if (!wait_all(&k_full[st], static_cast<uint32_t>(j / kKStages) & 1u)) return false;
         tc_fence_after();
-        const uint64_t dq = dq0 + static_cast<uint64_t>(w) * kTileUnits;
+        const uint64_t dq = dq0 + static_cast<uint64_t>(g.qtile(w)) * kTileUnits;
         const uint64_t dk = dk0 + static_cast<uint64_t>(st) * kTileUnits;
         const uint32_t ts = tmem_s(w);
 #pragma unroll
@@ -546,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&s_full[w]);
         // The last S MMA of tile j releases its K stage.
-        if (w == (j < g.nkt[1] ? 1 : 0)) mma_commit(&k_empty[st]);
+        if (w == g.last_user(j)) mma_commit(&k_empty[st]);
         return true;
       };
       // Stagger the two groups by half a period: group 1's first S is issued
@@ -554,28 +578,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       // group's softmax overlaps the other group's MMAs instead of both
       // groups contending for the exp unit while the tensor core idles.
       ok = wait_all(q_full, 0);
-      if (ok && g.nkt[0] > 0) ok = issue_s(0, 0);
-      else if (ok && g.nkt[1] > 0) ok = issue_s(1, 0);
-      for (int j = 0; ok && j < g.nmax; ++j) {
-        const int vst = j % kVStages;
-        const uint64_t dv = dv0 + static_cast<uint64_t>(vst) * kTileUnits;
-        const int w_last = j < g.nkt[1] ? 1 : 0;  // the last group that has tile j
-        bool v_ready = false;
+      if (ok && g.cnt[0] > 0) ok = issue_s(0, 0);
+      else if (ok && g.cnt[1] > 0) ok = issue_s(1, 0);
+      int v_ready = -1;  // the last key tile whose V has been waited for
+      const int rounds = max(g.cnt[0], g.cnt[1]);
+      for (int k = 0; ok && k < rounds; ++k) {
         for (int w = 0; ok && w < 2; ++w) {
-          if (j >= g.nkt[w]) continue;
-          if (!wait_all(&p_full[w], j & 1)) {
+          if (k >= g.cnt[w]) continue;
+          const int j = g.tile(w, k);
+          const int vst = j % kVStages;
+          const uint64_t dv = dv0 + static_cast<uint64_t>(vst) * kTileUnits;
+          if (!wait_all(&p_full[w], k & 1)) {
             ok = false;
             break;
           }
-          if (j == 0 && w == 0 && g.nkt[1] > 0 && !issue_s(1, 0)) {
+          if (k == 0 && w == 0 && g.cnt[1] > 0 && !issue_s(1, 0)) {
             ok = false;
             break;
           }
-          if (!v_ready && !wait_all(&v_full[vst], static_cast<uint32_t>(j / kVStages) & 1u)) {
+          if (v_ready != j && !wait_all(&v_full[vst], static_cast<uint32_t>(j / kVStages) & 1u)) {
             ok = false;
             break;
           }
-          v_ready = true;
+          v_ready = j;
           tc_fence_after();
           // P (bf16 pairs over S_w's first 64 columns) is the TMEM A operand;
           // 16 keys per step = 8 columns.  MMAs of this thread execute in
@@ -585,12 +610,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
             mma_bf16_ts(to, ts + kk * 8, dv + static_cast<uint64_t>(kk * 128), idesc_o,
-                        (j > 0 || kk > 0) ? 1u : 0u);
+                        (k > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&o_done[w]);
           // The tile's last P.V releases its V stage (before the next S is
           // issued, so the release does not wait for that S as well).
-          if (w == w_last) mma_commit(&v_empty[vst]);
-          if (j + 1 < g.nkt[w] && !issue_s(w, j + 1)) ok = false;
+          if (w == g.last_user(j)) mma_commit(&v_empty[vst]);
+          if (k + 1 < g.cnt[w] && !issue_s(w, k + 1)) ok = false;
         }
       }
       if (!ok && lane == 0) {
@@ -605,24 +630,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax
     const int w = wg;
+    const int qt = g.qtile(w);                         // this group's query tile
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const int iq = g.i0 + w * kBM + r;                 // this thread's query
+    const int iq = g.i0 + qt * kBM + r;                // this thread's query
     const int i = min(iq, sd.T - 1);                   // rows past T mirror the last query
     const int64_t qpos = prefix + i;
     // A warp whose 32 rows are all past T has nothing to compute (its rows of
     // P and O are never used); it only keeps the barrier protocol.
-    const bool warp_live = g.i0 + w * kBM + (warp & 3) * 32 < sd.T;
-    const int nkt = g.nkt[w];
+    const bool warp_live = g.i0 + qt * kBM + (warp & 3) * 32 < sd.T;
+    const int nk = g.cnt[w];
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(&s_full[w], j & 1)) {
+    for (int k = 0; k < nk; ++k) {
+      const int j = g.tile(w, k);
+      if (!mbar_wait(&s_full[w], k & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int64_t key0 = static_cast<int64_t>(j) * kBN;
-      const bool need_mask = key0 + kBN - 1 > prefix + g.i0 + w * kBM;  // some key may be masked
+      const bool need_mask = key0 + kBN - 1 > prefix + g.i0 + qt * kBM;  // some key may be masked
       float alpha = 1.f, m_use = m;
       bool rescale = false;
       // Keys c <= lim of this tile are visible to this row (int32, clamped).
@@ -664,8 +691,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Lazy rescale: keep the old max unless the new one exceeds it by
         // more than 8 (probabilities then stay below 2^8, exact in fp32).
         if (mx > m + 8.f) m_use = mx;
-        rescale = __any_sync(0xffffffffu, m_use != m) && j > 0;
-        alpha = ex2_approx(m - m_use);
+        rescale = __any_sync(0xffffffffu, m_use != m) && k > 0;
+        // (A row may see no key of its group's first tiles under the key
+        // split: m stays -inf and alpha must stay 1.)
+        alpha = m_use == m ? 1.f : ex2_approx(m - m_use);
       }
       if (warp_live) {
         // Pass 2: probabilities, written back as bf16 pairs over the S
@@ -676,11 +705,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         l = l * alpha + rsum;
         m = m_use;
       }
-      if (j > 0) {
+      if (k > 0) {
         // O is stable once the previous P.V completed (already the case once
         // S of this tile is complete: the MMAs complete in issue order).  The
         // rescale runs after pass 2, before this tile's P.V is issued.
-        if (!mbar_wait(&o_done[w], (j - 1) & 1)) {
+        if (!mbar_wait(&o_done[w], (k - 1) & 1)) {
           ok = false;
           break;
         }
@@ -701,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Zero V rows past the last valid key of the last tile (pool rows there
       // may be unwritten); the group issuing the tile's first P.V does it.
       const int64_t valid = g.total - key0;
-      const int first_w = j < g.nkt[0] ? 0 : 1;
+      const int first_w = g.split ? (j & 1) : (j < g.nkt[0] ? 0 : 1);
       if (w == first_w && valid < kBN) {
         // V of this tile must have landed before its rows are cleared.
         if (!mbar_wait(&v_full[j % kVStages], static_cast<uint32_t>(j / kVStages) & 1u)) {
@@ -722,36 +751,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&p_full[w]);
     }
-    if (nkt > 0) {
-      if (ok && !mbar_wait(&o_done[w], (nkt - 1) & 1)) ok = false;
-      if (!ok) {
-        if (r == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
-        *abort_flag = 1;
-      } else if (warp_live) {
-        tc_fence_after();
-        const float inv = 1.0f / l;
-        const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
+    if (nk > 0 && ok && !mbar_wait(&o_done[w], (nk - 1) & 1)) ok = false;
+    if (!ok) {
+      if (r == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
+      *abort_flag = 1;
+    }
+    // Row weights of the output: O_w / l in the two-query-tile case; under
+    // the key split group 0 writes (O_0 2^(m_0-M) + O_1 2^(m_1-M)) /
+    // (l_0 2^(m_0-M) + l_1 2^(m_1-M)), M = max(m_0, m_1).
+    bool write = ok && nk > 0 && warp_live;
+    float a_self = 1.f, a_other = 0.f, inv = 0.f;
+    if (g.split) {
+      // Group 1 hands its row max and sum over through its S columns, free
+      // once its last P.V has completed; group 0's thread r reads the same
+      // TMEM lane.  Both groups meet at named barrier 1 (256 threads).
+      if (w == 1 && write) {
+        tmem_st2(tmem_s(1) + lane_base, __float_as_uint(m), __float_as_uint(l));
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      tc_fence_after();
+      write = write && w == 0 && *reinterpret_cast<volatile int32_t*>(abort_flag) == 0;
+      if (write) {
+        uint32_t mb, lb;
+        tmem_ld2(tmem_s(1) + lane_base, mb, lb);
+        tmem_wait_ld();
+        const float m1 = __uint_as_float(mb), l1 = __uint_as_float(lb);
+        const float mm = fmaxf(m, m1);
+        a_self = ex2_approx(m - mm);
+        a_other = m1 == -INFINITY ? 0.f : ex2_approx(m1 - mm);
+        inv = 1.0f / (l * a_self + l1 * a_other);
+      }
+    } else if (write) {
+      inv = 1.0f / l;
+    }
+    if (write) {
+      tc_fence_after();
+      const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
+      const float ws = a_self * inv, wo = a_other * inv;
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          float o[32];
-          tmem_ld32(tmem_o(w) + lane_base + c, o);
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(tmem_o(w) + lane_base + c, o);
+        if (g.split) {
+          float o1[32];
+          tmem_ld32(tmem_o(1) + lane_base + c, o1);
           tmem_wait_ld();
-          if (iq < sd.T) {
-            const int64_t base = iq * sd.os0 + h * sd.os1 + c * sd.os2;
-            if (vec) {
 #pragma unroll
-              for (int e = 0; e < 32; e += 8) {
-                const uint4 wv = make_uint4(pack_bf16(o[e] * inv, o[e + 1] * inv),
-                                            pack_bf16(o[e + 2] * inv, o[e + 3] * inv),
-                                            pack_bf16(o[e + 4] * inv, o[e + 5] * inv),
-                                            pack_bf16(o[e + 6] * inv, o[e + 7] * inv));
-                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(sd.out) + base + e) = wv;
-              }
-            } else {
+          for (int e = 0; e < 32; ++e) o[e] = o[e] * ws + o1[e] * wo;
+        } else {
+          tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e)
-                store_elem(sd.out, base + e * sd.os2, p.out_dtype, o[e] * inv);
+          for (int e = 0; e < 32; ++e) o[e] *= ws;
+        }
+        if (iq < sd.T) {
+          const int64_t base = iq * sd.os0 + h * sd.os1 + c * sd.os2;
+          if (vec) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              const uint4 wv = make_uint4(pack_bf16(o[e], o[e + 1]), pack_bf16(o[e + 2], o[e + 3]),
+                                          pack_bf16(o[e + 4], o[e + 5]), pack_bf16(o[e + 6], o[e + 7]));
+              *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(sd.out) + base + e) = wv;
             }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) store_elem(sd.out, base + e * sd.os2, p.out_dtype, o[e]);
           }
         }
       }

@@ -117,9 +117,15 @@ def test_prefill_bf16_kv_against_oracle(prefix, T, seed):
     assert err <= 2e-2, f"max abs {err:.3e}"
 
 
+# One query tile with >= 2 key tiles takes the key split (the two softmax
+# groups alternate key tiles and merge at the end): (1000, 64), (600, 300)'s
+# last tile, (100, 64) where rows 0-27 see no key of group 1's first tile,
+# and (200, 100) with an odd key-tile count.
 @pytest.mark.parametrize("dim,bs,heads,prefix,T", [(64, 16, 4, 300, 130), (128, 8, 2, 40, 129),
                                                    (128, 32, 3, 1000, 64), (128, 256, 2, 600, 300),
-                                                   (64, 64, 5, 0, 1), (128, 16, 1, 127, 1)])
+                                                   (64, 64, 5, 0, 1), (128, 16, 1, 127, 1),
+                                                   (128, 16, 2, 100, 64), (64, 16, 3, 200, 100),
+                                                   (128, 8, 2, 129, 127)])
 @pytest.mark.parametrize("q_kind", ["f32", "bf16_strided"])
 def test_prefill_tensor_core_shapes(dim, bs, heads, prefix, T, q_kind):
     """fp32 q takes the thread-loaded Q path; bf16 q, here a strided view of a
