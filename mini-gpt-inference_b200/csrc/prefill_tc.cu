@@ -48,13 +48,22 @@ namespace {
 constexpr int kMaxSeqs = 64;   // sequences per launch (host splits larger batches)
 constexpr int kMaxWork = 2048; // (sequence, query pair) items per launch
 constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
-constexpr int kKStages = 3;    // K ring depth (K is needed first, by the S MMAs)
-constexpr int kVStages = 2;    // V ring depth (V is needed after the softmax)
 // Every kPolyEvery-th exponential pair of P runs on the FMA pipes (0: all on
 // MUFU; measured fastest while MUFU is not the limiting unit).
 constexpr int kPolyEvery = 0;
 constexpr int kBM = 128;       // queries per query tile (two tiles per CTA)
-constexpr int kBN = 128;       // keys per tile
+// Key-tile configurations.  BN = 64: S is double-buffered per query tile
+// (the MMAs of tile k+1 run during the softmax of tile k); used when the
+// launch has 256-query CTAs.  BN = 128: one S buffer, twice the keys per
+// barrier round trip and TMA burst; used when every CTA has a single query
+// tile (short chunks), where per-tile overheads dominate.
+template <int BN> struct TileCfg;
+template <> struct TileCfg<64> {
+  static constexpr int KS = 5, VS = 4, NBUF = 2;  // K / V ring depths, S buffers
+};
+template <> struct TileCfg<128> {
+  static constexpr int KS = 3, VS = 2, NBUF = 1;
+};
 
 struct SeqDesc {
   const void* q;
@@ -268,7 +277,7 @@ __device__ __forceinline__ uint32_t sw128(int r, int ch) {
 // written as bf16 pairs over the S columns already read (chunk [c, c+32) ->
 // P columns [c/2, c/2 + 16)).  The next 32-column chunk is loaded while the
 // current one is computed.  Returns the row sum of p.
-template <bool MASK>
+template <bool MASK, int kBN>
 __device__ __forceinline__ float p_pass(uint32_t srow, float scale, float neg_m, int lim) {
   const float2 sc2 = make_float2(scale, scale);
   const float2 nm2 = make_float2(neg_m, neg_m);
@@ -309,15 +318,20 @@ __device__ __forceinline__ float p_pass(uint32_t srow, float scale, float neg_m,
 }
 
 // Shared-memory layout (offsets from a 1024-aligned base).
-template <int D>
+template <int D, int kBN>
 struct Smem {
-  static constexpr int HALVES = D / 64;            // 64-element (128-byte) column halves
-  static constexpr int TILE = HALVES * 128 * 128;  // one 128-row operand tile
-  static constexpr int Q0 = 0;                     // Q tiles 0 and 1
-  static constexpr int K0 = Q0 + 2 * TILE;         // K ring
-  static constexpr int V0 = K0 + kKStages * TILE;  // V ring
-  static constexpr int BAR = V0 + kVStages * TILE;
-  static constexpr int BYTES = BAR + 256;
+  static constexpr int kKStages = TileCfg<kBN>::KS;
+  static constexpr int kVStages = TileCfg<kBN>::VS;
+  static constexpr int HALVES = D / 64;               // 64-element (128-byte) column halves
+  static constexpr int QHALF = kBM * 128;             // one column half of a Q tile
+  static constexpr int QTILE = HALVES * QHALF;        // a 128-query tile
+  static constexpr int KVHALF = kBN * 128;            // one column half of a K/V tile
+  static constexpr int KVTILE = HALVES * KVHALF;      // a 64-key tile
+  static constexpr int Q0 = 0;                        // Q tiles 0 and 1
+  static constexpr int K0 = Q0 + 2 * QTILE;           // K ring
+  static constexpr int V0 = K0 + kKStages * KVTILE;   // V ring
+  static constexpr int BAR = V0 + kVStages * KVTILE;
+  static constexpr int BYTES = BAR + 512;
 };
 
 // Loads query row i (zeros past T) of head h into row r of a swizzled Q tile.
@@ -370,11 +384,14 @@ struct Geom {
   __device__ int last_user(int j) const { return split ? (j & 1) : (j < nkt[1] ? 1 : 0); }
 };
 
-template <int D>
+template <int D, int kBN>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const __grid_constant__ PrefillParams p) {
-  using L = Smem<D>;
+  using L = Smem<D, kBN>;
+  constexpr int kKStages = TileCfg<kBN>::KS;
+  constexpr int kVStages = TileCfg<kBN>::VS;
+  constexpr int kNBuf = TileCfg<kBN>::NBUF;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
@@ -406,14 +423,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + kKStages;        // [kKStages]
   uint64_t* v_full = k_empty + kKStages;        // [kVStages]
   uint64_t* v_empty = v_full + kVStages;        // [kVStages]
-  uint64_t* s_full = v_empty + kVStages;        // [2] per query tile
-  uint64_t* p_full = s_full + 2;                // [2]
-  uint64_t* o_done = p_full + 2;                // [2]
-  uint64_t* mma_idle = o_done + 2;
+  // Per group w and tile parity b = k & 1 (index 2w + b): S(k) complete, P(k)
+  // written, P.V(k) complete.  A barrier of parity b completes once every
+  // other tile, and tile k+2 of a group cannot reach it before P.V(k) has
+  // been issued, so no waiter is ever two phases behind: every wait's parity
+  // is unambiguous even when some phases are never waited for.
+  uint64_t* s_full = v_empty + kVStages;        // [2 groups][2]
+  uint64_t* p_full = s_full + 4;                // [2 groups][2]
+  uint64_t* o_done = p_full + 4;                // [2 groups][2]
+  uint64_t* mma_idle = o_done + 4;
   uint64_t* q_full = mma_idle + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
   int32_t* abort_flag = reinterpret_cast<int32_t*>(q_full + 2);
-  static_assert((2 * kKStages + 2 * kVStages + 10) * 8 <= 256, "barrier area too small");
+  static_assert((2 * kKStages + 2 * kVStages + 16) * 8 <= 512, "barrier area too small");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
@@ -424,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < 4; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 128);
       mbar_init(&o_done[s], 1);
@@ -453,14 +475,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   // here by the softmax threads; either way the MMA issuer waits on q_full,
   // and K/V prefetch starts at once.
   if (!p.q_tma && wg >= 0) {
-    load_q_row<D>(smem + L::Q0 + wg * L::TILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
+    load_q_row<D>(smem + L::Q0 + wg * L::QTILE, r, g.i0 + wg * kBM + r, h, sd, p.q_dtype, p.q_vec);
     fence_proxy_async_shared();
     mbar_arrive(q_full);
   }
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [384,384+D).
-  auto tmem_s = [&](int w) { return tmem + static_cast<uint32_t>(w * 128); };
-  auto tmem_o = [&](int w) { return tmem + 256u + static_cast<uint32_t>(w * 128); };
+  // TMEM columns.  kBN = 64: group w has S buffers [256w, +64) and
+  // [256w+64, +64) and O [256w+128, +D).  kBN = 128: S_w [128w, +128),
+  // O_w [256+128w, +D).
+  auto tmem_s = [&](int w, int b) {
+    return tmem + static_cast<uint32_t>(kNBuf == 2 ? w * 256 + b * 64 : w * 128);
+  };
+  auto tmem_o = [&](int w) {
+    return tmem + static_cast<uint32_t>(kNBuf == 2 ? w * 256 + 128 : 256 + w * 128);
+  };
 
   if (warp == 0 || warp == 10) {
     // ------------------------------------------------------------ producers
@@ -481,10 +509,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(ntiles * L::HALVES * kBM * 128));
       for (int w = 0; w < ntiles; ++w)
         for (int half = 0; half < L::HALVES; ++half)
-          tma_load_3d(smem + L::Q0 + w * L::TILE + half * 16384, &p.qmap[seq], q_full, half * 64,
+          tma_load_3d(smem + L::Q0 + w * L::QTILE + half * L::QHALF, &p.qmap[seq], q_full, half * 64,
                       h, g.i0 + w * kBM);
     }
-    // A tile has at most 32 boxes (rbox >= 8, two column halves), so each
+    // A tile has at most 16 boxes (rbox >= 8, two column halves), so each
     // lane issues at most one: lane -> (block b, half).
     const int b = lane / L::HALVES;
     const int half = lane % L::HALVES;
@@ -522,9 +550,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * L::HALVES * box_bytes));
       __syncwarp();
       if (mine) {
-        uint8_t* dst = ring + st * L::TILE;
+        uint8_t* dst = ring + st * L::KVTILE;
         const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
-        tma_load_3d(dst + half * 16384 + b * p.rbox * 128, map, &full[st], half * 64, h, row);
+        tma_load_3d(dst + half * L::KVHALF + b * p.rbox * 128, map, &full[st], half * 64, h, row);
       }
       ++issued;
     }
@@ -545,41 +573,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
       };
-      constexpr uint32_t idesc_s = idesc_bf16(128, 128, false);
+      constexpr uint32_t idesc_s = idesc_bf16(128, kBN, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
       bool ok = true;
       // Descriptors of the tile bases; a step's descriptor adds its byte
       // offset / 16 to the 14-bit address field (no carry: smem < 256 KB).
       const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::Q0), 16, 1024);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::K0), 16, 1024);
-      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), 16384, 1024);
-      constexpr uint64_t kTileUnits = L::TILE >> 4;
-      // S of group w's k-th key tile.
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), L::KVHALF, 1024);
+      // S of group w's k-th key tile, into its S buffer k % kNBuf.
       auto issue_s = [&](int w, int k) -> bool {
         const int j = g.tile(w, k);
         const int st = j % kKStages;
         if (!wait_all(&k_full[st], static_cast<uint32_t>(j / kKStages) & 1u)) return false;
         tc_fence_after();
-        const uint64_t dq = dq0 + static_cast<uint64_t>(g.qtile(w)) * kTileUnits;
-        const uint64_t dk = dk0 + static_cast<uint64_t>(st) * kTileUnits;
-        const uint32_t ts = tmem_s(w);
+        const uint64_t dq = dq0 + static_cast<uint64_t>(g.qtile(w) * (L::QTILE >> 4));
+        const uint64_t dk = dk0 + static_cast<uint64_t>(st * (L::KVTILE >> 4));
+        const uint32_t ts = tmem_s(w, k % kNBuf);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
-          mma_bf16(ts, dq + koff, dk + koff, idesc_s, kk > 0 ? 1u : 0u);
+          const uint64_t qoff = static_cast<uint64_t>(((kk >> 2) * L::QHALF + (kk & 3) * 32) >> 4);
+          const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::KVHALF + (kk & 3) * 32) >> 4);
+          mma_bf16(ts, dq + qoff, dk + koff, idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[w]);
+        mma_commit(&s_full[w * 2 + (k & 1)]);
         // The last S MMA of tile j releases its K stage.
         if (w == g.last_user(j)) mma_commit(&k_empty[st]);
         return true;
       };
-      // Stagger the two groups by half a period: group 1's first S is issued
-      // only once group 0 has produced its first P, so from then on one
-      // group's softmax overlaps the other group's MMAs instead of both
-      // groups contending for the exp unit while the tensor core idles.
+      // Each group's first kNBuf S (all its S buffers) go out at once; after
+      // that S(k + kNBuf) follows P.V(k), which has read P(k) from the same
+      // buffer.  With two buffers the softmax of tile k+1 never waits for
+      // the MMAs of tile k.
       ok = wait_all(q_full, 0);
-      if (ok && g.cnt[0] > 0) ok = issue_s(0, 0);
-      else if (ok && g.cnt[1] > 0) ok = issue_s(1, 0);
+      for (int k = 0; k < kNBuf; ++k)
+        for (int w = 0; w < 2; ++w)
+          if (ok && k < g.cnt[w]) ok = issue_s(w, k);
       int v_ready = -1;  // the last key tile whose V has been waited for
       const int rounds = max(g.cnt[0], g.cnt[1]);
       for (int k = 0; ok && k < rounds; ++k) {
@@ -587,12 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (k >= g.cnt[w]) continue;
           const int j = g.tile(w, k);
           const int vst = j % kVStages;
-          const uint64_t dv = dv0 + static_cast<uint64_t>(vst) * kTileUnits;
-          if (!wait_all(&p_full[w], k & 1)) {
-            ok = false;
-            break;
-          }
-          if (k == 0 && w == 0 && g.cnt[1] > 0 && !issue_s(1, 0)) {
+          const uint64_t dv = dv0 + static_cast<uint64_t>(vst * (L::KVTILE >> 4));
+          if (!wait_all(&p_full[w * 2 + (k & 1)], static_cast<uint32_t>(k >> 1) & 1u)) {
             ok = false;
             break;
           }
@@ -606,16 +631,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 16 keys per step = 8 columns.  MMAs of this thread execute in
           // issue order, so S_w of the next tile is written only after this
           // P.V has read P.
-          const uint32_t to = tmem_o(w), ts = tmem_s(w);
+          const uint32_t to = tmem_o(w), ts = tmem_s(w, k % kNBuf);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
             mma_bf16_ts(to, ts + kk * 8, dv + static_cast<uint64_t>(kk * 128), idesc_o,
                         (k > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&o_done[w]);
+          mma_commit(&o_done[w * 2 + (k & 1)]);
           // The tile's last P.V releases its V stage (before the next S is
           // issued, so the release does not wait for that S as well).
           if (w == g.last_user(j)) mma_commit(&v_empty[vst]);
-          if (k + 1 < g.cnt[w] && !issue_s(w, k + 1)) ok = false;
+          if (k + kNBuf < g.cnt[w] && !issue_s(w, k + kNBuf)) ok = false;
         }
       }
       if (!ok && lane == 0) {
@@ -643,7 +668,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int k = 0; k < nk; ++k) {
       const int j = g.tile(w, k);
-      if (!mbar_wait(&s_full[w], k & 1)) {
+      const int sb = k & 1;          // barrier parity of this tile
+      const int buf = k % kNBuf;     // S buffer of this tile
+      if (!mbar_wait(&s_full[w * 2 + sb], static_cast<uint32_t>(k >> 1) & 1u)) {
         ok = false;
         break;
       }
@@ -662,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
           float sv[kBN];  // one TMEM round trip for the whole row
 #pragma unroll
-          for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s(w) + lane_base + c, sv + c);
+          for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s(w, buf) + lane_base + c, sv + c);
           tmem_wait_ld();
           // Eight independent chains of three-input max, then a tree.
           float mp[8];
@@ -700,21 +727,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Pass 2: probabilities, written back as bf16 pairs over the S
         // columns already consumed; the masked variant is a separate
         // instantiation so unmasked tiles carry no per-element selects.
-        const float rsum = need_mask ? p_pass<true>(tmem_s(w) + lane_base, p.scale_log2, -m_use, lim)
-                                     : p_pass<false>(tmem_s(w) + lane_base, p.scale_log2, -m_use, lim);
+        const uint32_t srow = tmem_s(w, buf) + lane_base;
+        const float rsum = need_mask ? p_pass<true, kBN>(srow, p.scale_log2, -m_use, lim)
+                                     : p_pass<false, kBN>(srow, p.scale_log2, -m_use, lim);
         l = l * alpha + rsum;
         m = m_use;
       }
-      if (k > 0) {
-        // O is stable once the previous P.V completed (already the case once
-        // S of this tile is complete: the MMAs complete in issue order).  The
-        // rescale runs after pass 2, before this tile's P.V is issued.
-        if (!mbar_wait(&o_done[w], (k - 1) & 1)) {
+      if (rescale) {
+        // P.V(k-1) must have completed before O is rescaled (only then is
+        // the softmax held back by the MMAs of an earlier tile).
+        const int kp = k - 1;
+        if (!mbar_wait(&o_done[w * 2 + (kp & 1)], static_cast<uint32_t>(kp >> 1) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (warp_live && rescale) {
+        if (warp_live) {
 #pragma unroll
           for (int c = 0; c < D; c += 32) {
             float o[32];
@@ -738,20 +766,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      if (w == first_w && valid < kBN && r >= valid) {
-        uint8_t* vrow = smem + L::V0 + (j % kVStages) * L::TILE + r * 128;
+      if (w == first_w && valid < kBN && r >= valid && r < kBN) {
+        uint8_t* vrow = smem + L::V0 + (j % kVStages) * L::KVTILE + r * 128;
 #pragma unroll
         for (int half = 0; half < L::HALVES; ++half)
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<uint4*>(vrow + half * 16384 + ((ch ^ (r & 7)) << 4)) =
+            *reinterpret_cast<uint4*>(vrow + half * L::KVHALF + ((ch ^ (r & 7)) << 4)) =
                 make_uint4(0, 0, 0, 0);
         fence_proxy_async_shared();
       }
       tc_fence_before();
-      mbar_arrive(&p_full[w]);
+      mbar_arrive(&p_full[w * 2 + sb]);
     }
-    if (nk > 0 && ok && !mbar_wait(&o_done[w], (nk - 1) & 1)) ok = false;
+    // The last P.V completing implies all earlier ones have (issue order).
+    if (nk > 0 && ok &&
+        !mbar_wait(&o_done[w * 2 + ((nk - 1) & 1)], static_cast<uint32_t>((nk - 1) >> 1) & 1u))
+      ok = false;
     if (!ok) {
       if (r == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
       *abort_flag = 1;
@@ -766,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // once its last P.V has completed; group 0's thread r reads the same
       // TMEM lane.  Both groups meet at named barrier 1 (256 threads).
       if (w == 1 && write) {
-        tmem_st2(tmem_s(1) + lane_base, __float_as_uint(m), __float_as_uint(l));
+        tmem_st2(tmem_s(1, 0) + lane_base, __float_as_uint(m), __float_as_uint(l));
         tmem_wait_st();
       }
       tc_fence_before();
@@ -776,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       write = write && w == 0 && *reinterpret_cast<volatile int32_t*>(abort_flag) == 0;
       if (write) {
         uint32_t mb, lb;
-        tmem_ld2(tmem_s(1) + lane_base, mb, lb);
+        tmem_ld2(tmem_s(1, 0) + lane_base, mb, lb);
         tmem_wait_ld();
         const float m1 = __uint_as_float(mb), l1 = __uint_as_float(lb);
         const float mm = fmaxf(m, m1);
@@ -841,15 +872,14 @@ bool prefill_tc_supported(const b200_prefill_args_t& a) {
   return true;
 }
 
-int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream) {
-  if (n <= 0) return B200_OK;
-  DeviceInfo dev;
-  int rc = current_device_info(&dev);
-  if (rc != B200_OK) return rc;
+template <int D_, int BN>
+int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
+              const DeviceInfo& dev) {
+  int rc = B200_OK;
   const b200_prefill_args_t& a0 = seqs[0];
   const int64_t D = a0.pool.head_dim, H = a0.pool.num_heads, S = a0.pool.block_size;
   const int64_t P = a0.pool.num_blocks, Ly = a0.pool.num_layers;
-  const size_t smem = static_cast<size_t>(D == 128 ? Smem<128>::BYTES : Smem<64>::BYTES) + 1024;
+  const size_t smem = static_cast<size_t>(Smem<D_, BN>::BYTES) + 1024;
   if (smem > static_cast<size_t>(dev.max_smem_optin))
     return fail(B200_ERR_UNSUPPORTED, "tensor-core prefill: not enough shared memory");
 
@@ -857,7 +887,7 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
   const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H),
                             static_cast<uint64_t>(Ly * P * S)};
   const uint64_t strides[2] = {static_cast<uint64_t>(D * 2), static_cast<uint64_t>(H * D * 2)};
-  const int64_t rbox = std::min<int64_t>(S, kBN);
+  const int64_t rbox = std::min<int64_t>(S, BN);
   const uint32_t box[3] = {64u, 1u, static_cast<uint32_t>(rbox)};
   rc = encode_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a0.pool.k, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
@@ -866,18 +896,13 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B200_OK) return rc;
 
-  static int configured[64][2] = {{0}};
-  const int slot = D == 128 ? 1 : 0;
-  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device][slot]) {
-    cudaError_t e = D == 128
-                        ? cudaFuncSetAttribute(prefill_tc_kernel<128>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem))
-                        : cudaFuncSetAttribute(prefill_tc_kernel<64>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem));
+  static int configured[64] = {0};
+  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<D_, BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
-    configured[dev.device][slot] = 1;
+    configured[dev.device] = 1;
   }
 
   for (int64_t base = 0; base < n; base += kMaxSeqs) {
@@ -967,7 +992,7 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
         for (int w = 0; w < 2; ++w) {
           const int64_t lo = qp * 2 * kBM + w * kBM;
           if (lo < s.num_tokens)
-            tiles += ceil_div(s.prefix_len + std::min<int64_t>(s.num_tokens, lo + kBM), kBN);
+            tiles += ceil_div(s.prefix_len + std::min<int64_t>(s.num_tokens, lo + kBM), BN);
         }
         items.emplace_back(tiles, static_cast<uint32_t>(i) | (static_cast<uint32_t>(qp) << 8));
       }
@@ -978,15 +1003,30 @@ int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t s
       const size_t nw = std::min<size_t>(kMaxWork, items.size() - w0);
       for (size_t k = 0; k < nw; ++k) prm.work[k] = items[w0 + k].second;
       const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw));
-      if (D == 128)
-        prefill_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
-      else
-        prefill_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
+      prefill_tc_kernel<D_, BN><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "prefill_tc launch");
     }
   }
   return B200_OK;
+}
+
+
+int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return B200_OK;
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != B200_OK) return rc;
+  // 128-key tiles when every CTA holds a single query tile, else 64-key tiles
+  // with double-buffered S.
+  int64_t max_t = 0;
+  for (int64_t i = 0; i < n; ++i) max_t = std::max<int64_t>(max_t, seqs[i].num_tokens);
+  const bool short_chunks = max_t <= kBM;
+  if (seqs[0].pool.head_dim == 128)
+    return short_chunks ? launch_tc<128, 128>(seqs, n, stream, dev)
+                        : launch_tc<128, 64>(seqs, n, stream, dev);
+  return short_chunks ? launch_tc<64, 128>(seqs, n, stream, dev)
+                      : launch_tc<64, 64>(seqs, n, stream, dev);
 }
 
 }  // namespace b200

@@ -181,3 +181,38 @@ def test_prefill_batch_matches_single_calls():
         single = chunked_prefill_b200(q, pool, t, c.prefix_len, 0)
         torch.cuda.synchronize()
         assert torch.equal(single.cpu(), o.cpu())
+
+
+def test_prefill_batch_mixed_chunk_lengths_against_oracle():
+    """A batch holding a chunk longer than one query tile runs every sequence
+    with 64-key tiles and double-buffered S; a batch of short chunks runs
+    128-key tiles.  Both must match the fp32 oracle."""
+    from b200attn import chunked_prefill_batch_b200, kv_scatter_b200
+
+    d = _dev()
+    for specs in ([(100, 64, 21), (640, 300, 22), (0, 129, 23)], [(100, 64, 24), (33, 1, 25)]):
+        cs = [cases.prefill_case(p, t, 4, 128, 16, s, dtype=torch.bfloat16, n_layer=1,
+                                 layer_idx=0) for p, t, s in specs]
+        S = 16
+        sizes = [c.pool.k.shape[1] for c in cs]
+        kp = torch.cat([c.pool.k for c in cs], dim=1)
+        vp = torch.cat([c.pool.v for c in cs], dim=1)
+        pool = cases.Pool(kp.to(d), vp.to(d), S)
+        tables, qs, offs, wants = [], [], 0, []
+        for c, n in zip(cs, sizes):
+            table = [x + offs for x in c.block_table]
+            slots = [s + offs * S for s in c.slots]
+            kv_scatter_b200(c.k.to(d), c.v.to(d), pool, slots, 0)
+            k2, v2 = c.pool.k.clone(), c.pool.v.clone()
+            oracle.kv_scatter(k2, v2, c.k, c.v, c.slots, 0)
+            wants.append(oracle.prefix_prefill_from_pool(c.q.float(), k2.float(), v2.float(),
+                                                         c.block_table, c.prefix_len, 0,
+                                                         compute_dtype=torch.float64).float())
+            tables.append(table)
+            qs.append(c.q.to(d))
+            offs += n
+        outs = chunked_prefill_batch_b200(qs, pool, tables, [c.prefix_len for c in cs], 0)
+        torch.cuda.synchronize()
+        for o, want in zip(outs, wants):
+            err = (o.float().cpu() - want).abs().max().item()
+            assert err <= 2e-2, f"max abs {err:.3e}"
