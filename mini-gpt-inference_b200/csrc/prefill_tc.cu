@@ -47,7 +47,7 @@ namespace {
 
 constexpr int kMaxSeqs = 64;   // sequences per launch (host splits larger batches)
 constexpr int kMaxWork = 2048; // (sequence, query pair) items per launch
-constexpr int kThreads = 352;  // K producer, MMA, two 4-warp softmax groups, V producer
+constexpr int kThreads = 384;  // K producer, S issuer, two 4-warp softmax groups, V producer, P.V issuer
 // Every kPolyEvery-th exponential pair of P runs on the FMA pipes (0: all on
 // MUFU; measured fastest while MUFU is not the limiting unit).
 constexpr int kPolyEvery = 0;
@@ -431,11 +431,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + kVStages;        // [2 groups][2]
   uint64_t* p_full = s_full + 4;                // [2 groups][2]
   uint64_t* o_done = p_full + 4;                // [2 groups][2]
-  uint64_t* mma_idle = o_done + 4;
-  uint64_t* q_full = mma_idle + 1;
+  uint64_t* mma_idle = o_done + 4;              // [2]: S issuer, P.V issuer
+  uint64_t* q_full = mma_idle + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
   int32_t* abort_flag = reinterpret_cast<int32_t*>(q_full + 2);
-  static_assert((2 * kKStages + 2 * kVStages + 16) * 8 <= 512, "barrier area too small");
+  static_assert((2 * kKStages + 2 * kVStages + 17) * 8 <= 512, "barrier area too small");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
@@ -451,7 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[s], 128);
       mbar_init(&o_done[s], 1);
     }
-    mbar_init(mma_idle, 1);
+    mbar_init(&mma_idle[0], 1);
+    mbar_init(&mma_idle[1], 1);
     mbar_init(q_full, p.q_tma ? 1 : 256);
     *abort_flag = 0;
     fence_mbar_init();
@@ -565,22 +566,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       if (is_k && p.q_tma && !mbar_wait(q_full, 0)) report(p.status, B200_DEV_WAIT_TIMEOUT);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs the issue loop (values stay warp-uniform); every
-    // lane waits on the barriers itself and a vote makes the outcome uniform.
-    {
-      auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-        return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
-      };
+  } else if (warp == 1 || warp == 11) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 1 issues every S (and releases K stages), warp 11 every P.V (and
+    // releases V stages), so that one issuer's barrier waits and commits
+    // overlap the other's MMAs.  Each runs its loop as a whole warp (values
+    // stay warp-uniform); every lane waits on the barriers itself and a vote
+    // makes the outcome uniform; elect.sync picks the issuing lane.
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+    };
+    bool ok = true;
+    // Descriptors of the tile bases; a step's descriptor adds its byte
+    // offset / 16 to the 14-bit address field (no carry: smem < 256 KB).
+    if (warp == 1) {
       constexpr uint32_t idesc_s = idesc_bf16(128, kBN, false);
-      constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
-      bool ok = true;
-      // Descriptors of the tile bases; a step's descriptor adds its byte
-      // offset / 16 to the 14-bit address field (no carry: smem < 256 KB).
       const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::Q0), 16, 1024);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::K0), 16, 1024);
-      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), L::KVHALF, 1024);
       // S of group w's k-th key tile, into its S buffer k % kNBuf.
       auto issue_s = [&](int w, int k) -> bool {
         const int j = g.tile(w, k);
@@ -601,14 +603,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (w == g.last_user(j)) mma_commit(&k_empty[st]);
         return true;
       };
-      // Each group's first kNBuf S (all its S buffers) go out at once; after
-      // that S(k + kNBuf) follows P.V(k), which has read P(k) from the same
-      // buffer.  With two buffers the softmax of tile k+1 never waits for
-      // the MMAs of tile k.
+      // Each group's first kNBuf S (all its S buffers) go out at once.  S(k)
+      // for k >= kNBuf overwrites P(k - kNBuf), so it waits for that P.V to
+      // complete (every o_done phase is waited for here, in order).  With two
+      // buffers the softmax of tile k+1 never waits for the MMAs of tile k.
       ok = wait_all(q_full, 0);
       for (int k = 0; k < kNBuf; ++k)
         for (int w = 0; w < 2; ++w)
           if (ok && k < g.cnt[w]) ok = issue_s(w, k);
+      const int rounds = max(g.cnt[0], g.cnt[1]);
+      for (int k = kNBuf; ok && k < rounds; ++k) {
+        for (int w = 0; ok && w < 2; ++w) {
+          if (k >= g.cnt[w]) continue;
+          const int kp = k - kNBuf;
+          if (!wait_all(&o_done[w * 2 + (kp & 1)], static_cast<uint32_t>(kp >> 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!issue_s(w, k)) ok = false;
+        }
+      }
+    } else {
+      constexpr uint32_t idesc_o = idesc_bf16(128, D, true);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), L::KVHALF, 1024);
       int v_ready = -1;  // the last key tile whose V has been waited for
       const int rounds = max(g.cnt[0], g.cnt[1]);
       for (int k = 0; ok && k < rounds; ++k) {
@@ -627,30 +645,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           v_ready = j;
           tc_fence_after();
-          // P (bf16 pairs over S_w's first 64 columns) is the TMEM A operand;
-          // 16 keys per step = 8 columns.  MMAs of this thread execute in
-          // issue order, so S_w of the next tile is written only after this
-          // P.V has read P.
+          // P (bf16 pairs over S_w's first columns) is the TMEM A operand;
+          // 16 keys per step = 8 columns.
           const uint32_t to = tmem_o(w), ts = tmem_s(w, k % kNBuf);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
             mma_bf16_ts(to, ts + kk * 8, dv + static_cast<uint64_t>(kk * 128), idesc_o,
                         (k > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&o_done[w * 2 + (k & 1)]);
-          // The tile's last P.V releases its V stage (before the next S is
-          // issued, so the release does not wait for that S as well).
+          // The tile's last P.V releases its V stage.
           if (w == g.last_user(j)) mma_commit(&v_empty[vst]);
-          if (k + kNBuf < g.cnt[w] && !issue_s(w, k + kNBuf)) ok = false;
         }
       }
-      if (!ok && lane == 0) {
-        report(p.status, B200_DEV_WAIT_TIMEOUT);
-        *abort_flag = 1;
-      }
-      // Wait until every MMA the warp issued has completed.
-      mma_commit(mma_idle);
-      if (!wait_all(mma_idle, 0) && lane == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
     }
+    if (!ok && lane == 0) {
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+      *abort_flag = 1;
+    }
+    // Wait until every MMA this warp issued has completed.
+    uint64_t* idle = &mma_idle[warp == 1 ? 0 : 1];
+    mma_commit(idle);
+    if (!wait_all(idle, 0) && lane == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
