@@ -33,6 +33,60 @@ struct ScatterParams {
   int32_t* status;
 };
 
+// Same-dtype copy of tokens whose H*D run is contiguous in k, v and the pool
+// (q/k/v views of a fused projection have head stride D): a flat 16-byte
+// copy of H*D*es bytes per tensor.  Each thread issues all of its loads (up
+// to kFlatIter chunks of k and of v) before its stores, with streaming
+// cache hints (the data is read and written once).
+constexpr int kFlatIter = 4;
+struct FlatParams {
+  int64_t P, S;
+  int64_t layer_row0;
+  int64_t run;        // 16-byte chunks per token per tensor
+  int64_t k_tok, v_tok;  // token stride of k / v in 16-byte chunks
+  const uint4* k;
+  const uint4* v;
+  uint4* kp;
+  uint4* vp;
+  const void* slots;
+  int64_t ss;
+  int32_t slots_i64;
+  int32_t* status;
+};
+
+__global__ void __launch_bounds__(256) kv_scatter_flat_kernel(const FlatParams p) {
+  const int64_t n = blockIdx.x;
+  const int64_t slot = load_index(p.slots, n * p.ss, p.slots_i64);
+  if (slot < 0 || slot >= p.P * p.S) {
+    if (threadIdx.x == 0) report(p.status, B200_DEV_BAD_SLOT);
+    return;
+  }
+  const uint4* ks = p.k + n * p.k_tok;
+  const uint4* vs = p.v + n * p.v_tok;
+  uint4* kd = p.kp + (p.layer_row0 + slot) * p.run;
+  uint4* vd = p.vp + (p.layer_row0 + slot) * p.run;
+  const int run = static_cast<int>(p.run);
+  for (int base = threadIdx.x; base < run; base += kFlatIter * blockDim.x) {
+    uint4 a[kFlatIter], b[kFlatIter];
+#pragma unroll
+    for (int i = 0; i < kFlatIter; ++i) {
+      const int c = base + i * blockDim.x;
+      if (c < run) {
+        a[i] = __ldcs(ks + c);
+        b[i] = __ldcs(vs + c);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kFlatIter; ++i) {
+      const int c = base + i * blockDim.x;
+      if (c < run) {
+        __stcs(kd + c, a[i]);
+        __stcs(vd + c, b[i]);
+      }
+    }
+  }
+}
+
 template <typename PoolT>
 struct Pack;
 template <>
@@ -163,9 +217,37 @@ int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream) {
            ((st[0] * es) % 16) == 0 && ((st[1] * es) % 16) == 0 && (ne * es) % 16 == 0;
   };
   p.vec_ok = (a.kv_in_dtype != B200_DTYPE_F16) && aligned(a.k, a.k_stride) && aligned(a.v, a.v_stride);
+  if (p.N > 0x7fffffffLL) return fail(B200_ERR_UNSUPPORTED, "kv_scatter: too many tokens");
+  // Flat path: same dtype, each token's H*D run contiguous in k, v and the
+  // pool, 16-byte aligned rows (checked by vec_ok) and a run of whole chunks.
+  const int64_t run_bytes = p.H * p.D * static_cast<int64_t>(es);
+  if (p.vec_ok && a.kv_in_dtype == a.pool.dtype && a.k_stride[1] == p.D &&
+      a.v_stride[1] == p.D && run_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(a.pool.k) % 16) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.pool.v) % 16) == 0) {
+    FlatParams f{};
+    f.P = p.P;
+    f.S = p.S;
+    f.layer_row0 = p.layer_row0;
+    f.run = run_bytes / 16;
+    f.k_tok = a.k_stride[0] * static_cast<int64_t>(es) / 16;
+    f.v_tok = a.v_stride[0] * static_cast<int64_t>(es) / 16;
+    f.k = static_cast<const uint4*>(a.k);
+    f.v = static_cast<const uint4*>(a.v);
+    f.kp = static_cast<uint4*>(a.pool.k);
+    f.vp = static_cast<uint4*>(a.pool.v);
+    f.slots = a.slot_mapping;
+    f.ss = a.slot_stride;
+    f.slots_i64 = p.slots_i64;
+    f.status = a.status;
+    const int threads = static_cast<int>(std::min<int64_t>(
+        256, std::max<int64_t>(32, (f.run + kFlatIter - 1) / kFlatIter + 31) / 32 * 32));
+    kv_scatter_flat_kernel<<<static_cast<unsigned>(p.N), threads, 0, stream>>>(f);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "kv_scatter launch");
+    return B200_OK;
+  }
   const int64_t chunks = p.H * ((p.D + ne - 1) / ne);
   const int threads = chunks >= 256 ? 256 : static_cast<int>((chunks + 31) / 32 * 32);
-  if (p.N > 0x7fffffffLL) return fail(B200_ERR_UNSUPPORTED, "kv_scatter: too many tokens");
   const unsigned blocks = static_cast<unsigned>(p.N);
   if (a.pool.dtype == B200_DTYPE_F32)
     kv_scatter_kernel<float><<<blocks, threads, 0, stream>>>(p);
