@@ -379,6 +379,22 @@ def gpu_indices(world: int) -> list:
 
 
 # ------------------------------------------------------------------ CPU leg
+def usable_cpus() -> int:
+    """CPUs this process may run on: the affinity mask, capped by a cgroup
+    v2 CPU quota when one is set (os.cpu_count() sees neither)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        quota, period = Path("/sys/fs/cgroup/cpu.max").read_text().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, math.ceil(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
 def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
     """Times the reference algorithm (its CPU restatement under oracle/) on
     the host cores, all threads, on a bounded sample of the workload."""
@@ -386,7 +402,7 @@ def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
     import oracle
     from b200attn.ops import decode_bytes
 
-    threads = os.cpu_count() or 1
+    threads = usable_cpus()
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(5)
     if workload in ("cfg4", "cfg3"):
@@ -535,7 +551,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         nbytes = wl.bytes() if hasattr(wl, "bytes") else wl.work()
         achieved, r_unit = nbytes / per_launch_s / 1e9, "GB/s"
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    # The CPU baseline is an N=1 figure (under torchrun the other ranks would
+    # wait for it in the closing barrier).
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_sample(args.workload, steps=3, warmup=0)
         cpu.pop("seconds_per_step")
     if rank == 0:
