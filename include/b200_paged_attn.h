@@ -244,6 +244,16 @@ B200_API size_t b200_chunked_prefill_workspace_size(int64_t num_tokens, int64_t 
  * and returns its full length. */
 B200_API size_t b200_last_error(char* buf, size_t len);
 
+/*
+ * Failure-path self-test.  No counterpart in the reference: it exercises,
+ * on the device, the bounded waits every kernel pipeline uses.  One warp
+ * waits (through the same wait routine) on a barrier phase that nothing
+ * completes; after limit_ns (0 < limit_ns <= 2e9) the kernel ORs
+ * B200_DEV_WAIT_TIMEOUT into *status (a device word) and returns normally,
+ * so the context stays usable.  Nothing faults, traps or hangs.
+ */
+B200_API int b200_selftest_bounded_wait(int32_t* status, int64_t limit_ns, void* stream);
+
 /* ABI version and the compute capability the library was built for. */
 B200_API int b200_abi_version(void);
 B200_API int b200_built_arch(void);

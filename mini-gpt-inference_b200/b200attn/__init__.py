@@ -5,12 +5,15 @@ Public API (CUDA only, no fallback):
   kv_scatter_b200             -- slot-mapping KV-cache scatter
   chunked_prefill_b200        -- prefix-aware chunked-prefill attention
   chunked_prefill_batch_b200  -- several prefill chunks in one launch
+  selftest_bounded_wait       -- device check of the kernels' bounded-wait error path
 """
 from .ops import (chunked_prefill_b200, chunked_prefill_batch_b200, decode_bytes,
-                  is_available, kv_scatter_b200, paged_attention_batch_b200)
+                  is_available, kv_scatter_b200, paged_attention_batch_b200,
+                  selftest_bounded_wait)
 from ._lib import LIB_PATH, load as load_library
 
 __all__ = [
     "paged_attention_batch_b200", "kv_scatter_b200", "chunked_prefill_b200",
-    "chunked_prefill_batch_b200", "decode_bytes", "is_available", "load_library", "LIB_PATH",
+    "chunked_prefill_batch_b200", "selftest_bounded_wait", "decode_bytes", "is_available",
+    "load_library", "LIB_PATH",
 ]

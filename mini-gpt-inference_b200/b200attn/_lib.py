@@ -88,6 +88,7 @@ SIGNATURES = {
     "b200_chunked_prefill_workspace_size": (
         ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int]),
     "b200_last_error": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
+    "b200_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_void_p, _i64, _p]),
     "b200_abi_version": (ctypes.c_int, []),
     "b200_built_arch": (ctypes.c_int, []),
 }

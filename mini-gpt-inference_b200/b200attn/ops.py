@@ -412,3 +412,16 @@ def decode_bytes(context_lengths: Sequence[int], num_heads: int, head_dim: int,
     if fused_in_bytes:
         total += B * num_heads * head_dim * 2 * (fused_in_bytes + kv_bytes) + B * idx_bytes
     return total
+
+
+def selftest_bounded_wait(limit_ns: int = 10_000_000, device=None) -> int:
+    """Runs the device self-test of the bounded-wait error path: one warp
+    waits, through the kernels' own wait routine, on a barrier phase that
+    nothing completes; after ``limit_ns`` it gives up, sets
+    B200_DEV_WAIT_TIMEOUT and returns.  Returns the status word."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(lib.b200_selftest_bounded_wait(status.data_ptr(), int(limit_ns), _stream_ptr(dev)),
+               "bounded-wait selftest")
+    return int(status.item())

@@ -142,6 +142,14 @@ using namespace b200;
 extern "C" {
 
 int b200_abi_version(void) { return B200_PAGED_ATTN_ABI_VERSION; }
+
+int b200_selftest_bounded_wait(int32_t* status, int64_t limit_ns, void* stream) {
+  clear_error();
+  if (status == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "selftest: status must be a device word");
+  if (limit_ns <= 0 || limit_ns > 2000000000LL)
+    return fail(B200_ERR_INVALID_ARGUMENT, "selftest: limit_ns must be in (0, 2e9]");
+  return launch_bounded_wait_selftest(status, limit_ns, static_cast<cudaStream_t>(stream));
+}
 int b200_built_arch(void) { return 100; }
 
 size_t b200_last_error(char* buf, size_t len) {

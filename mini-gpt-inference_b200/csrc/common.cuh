@@ -110,14 +110,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false
-// (and never blocks longer than kWaitLimitNs) when it does not.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// (and never blocks much longer than limit_ns) when it does not.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((i & 31u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 31u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

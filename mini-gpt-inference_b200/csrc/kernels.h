@@ -16,6 +16,8 @@ int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream);
 // tcgen05 prefill over `n` sequences sharing one pool (bf16, D in {64,128}).
 int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream);
 bool prefill_tc_supported(const b200_prefill_args_t& a);
+// One warp waiting on an mbarrier nothing arrives on, with the given limit.
+int launch_bounded_wait_selftest(int32_t* status, int64_t limit_ns, cudaStream_t stream);
 
 // Split-K planning shared by the launcher and the workspace query.
 int64_t decode_tiles_per_split(int64_t units, int64_t max_tiles, int32_t hint, int num_sms);

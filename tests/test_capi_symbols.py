@@ -81,3 +81,13 @@ def test_ops_reject_cpu_tensors_loudly():
     c = cases.cfg1_case()
     with pytest.raises(ValueError, match="CUDA"):
         paged_attention_batch_b200(c.q, c.pool, c.block_tables, c.context_lengths, 0)
+
+
+def test_selftest_rejects_bad_arguments_without_gpu():
+    from b200attn import _lib
+
+    lib = _lib.load()
+    # Validation happens on the host before any CUDA call.
+    assert lib.b200_selftest_bounded_wait(None, 1000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.b200_selftest_bounded_wait(8, 0, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.b200_selftest_bounded_wait(8, 3_000_000_000, None) == _lib.ERR_INVALID_ARGUMENT
