@@ -42,12 +42,12 @@ def run_mode(mode: str, a) -> dict:
                        policy="conservative", n_head=a.heads, head_dim=128,
                        device_tables=mode != "eager", graphs=mode == "graphs")
     rt.sync_cuda_timing = True
-    if mode == "graphs":
-        rt.runner.graphs.capture_all()  # capture outside the timed steps
     for r in reqs:
         rt.add_request(r)
-    t0 = time.perf_counter()
     with torch.inference_mode():
+        if mode == "graphs":
+            rt.runner.graphs.capture_all()  # capture outside the timed steps
+        t0 = time.perf_counter()
         rt.run_to_completion(reqs, max_steps=100_000)
     wall = time.perf_counter() - t0
     dec = [x for x in rt.records if x.decode_tokens > 0]

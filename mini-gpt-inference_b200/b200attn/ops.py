@@ -44,6 +44,14 @@ def is_available() -> bool:
     return torch.cuda.is_available()
 
 
+def _inference_only(*tensors) -> None:
+    """The ops have no backward: like the reference's triton_v0 branch
+    (minivllm/attention.py:404-405) they refuse inputs that require grad
+    while grad mode is on."""
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
+        raise RuntimeError("the b200 backend is inference-only; run under torch.inference_mode()")
+
+
 def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -143,6 +151,7 @@ def paged_attention_batch_b200(q: torch.Tensor, pool, block_tables: torch.Tensor
     Returns a fresh [B, H, D] tensor of q.dtype (or fills ``out``); with
     prepare=True returns a PreparedCall that launches it.
     """
+    _inference_only(q, k_new, v_new)
     lib = _lib.load()
     if not q.is_cuda:
         raise ValueError("CUDA q required for the b200 backend")
@@ -235,6 +244,7 @@ def kv_scatter_b200(k: torch.Tensor, v: torch.Tensor, pool, slot_mapping,
     k, v: [N, H, D] (any strides, any float dtype; converted to the pool's);
     slot_mapping: [N] integer CUDA tensor or a host sequence of ints.
     """
+    _inference_only(k, v)
     lib = _lib.load()
     if not k.is_cuda:
         raise ValueError("CUDA k/v required for the b200 backend")
@@ -324,6 +334,7 @@ def chunked_prefill_b200(q: torch.Tensor, pool, block_table, prefix_len: int,
     must already be in the pool (see :func:`kv_scatter_b200`).
     Returns [T, H, D] in q.dtype.
     """
+    _inference_only(q)
     lib = _lib.load()
     _check_prefill_inputs(q, pool, prefix_len, layer_idx)
     pstruct = _pool_struct(pool)
@@ -368,6 +379,7 @@ def chunked_prefill_batch_b200(qs: Sequence[torch.Tensor], pool, block_tables: S
     keep = []
     total_ws = 0
     for i, (q, bt, pl) in enumerate(zip(qs, block_tables, prefix_lens)):
+        _inference_only(q)
         _check_prefill_inputs(q, pool, pl, layer_idx)
         if q.device != dev or q.dtype != qs[0].dtype:
             raise ValueError("batched prefill chunks must share device and dtype")

@@ -91,3 +91,26 @@ def test_selftest_rejects_bad_arguments_without_gpu():
     assert lib.b200_selftest_bounded_wait(None, 1000, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.b200_selftest_bounded_wait(8, 0, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.b200_selftest_bounded_wait(8, 3_000_000_000, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_ops_are_inference_only():
+    """Inputs that require grad are refused while grad mode is on (as the
+    reference's triton_v0 branch does, minivllm/attention.py:404-405), before
+    any device check, so this runs on CPU."""
+    from types import SimpleNamespace
+
+    from b200attn import chunked_prefill_b200, kv_scatter_b200, paged_attention_batch_b200
+
+    q = torch.zeros(2, 2, 8, requires_grad=True)
+    pool = SimpleNamespace(k=torch.zeros(1, 2, 4, 2, 8), v=torch.zeros(1, 2, 4, 2, 8), block_size=4)
+    with pytest.raises(RuntimeError, match="inference-only"):
+        paged_attention_batch_b200(q, pool, torch.zeros(2, 1, dtype=torch.long),
+                                   torch.ones(2, dtype=torch.long), 0)
+    with pytest.raises(RuntimeError, match="inference-only"):
+        chunked_prefill_b200(q, pool, [0], 0, 0)
+    with pytest.raises(RuntimeError, match="inference-only"):
+        kv_scatter_b200(q, q, pool, [0, 1], 0)
+    with torch.inference_mode():  # no grad mode: the CUDA check comes next
+        with pytest.raises(ValueError, match="CUDA"):
+            paged_attention_batch_b200(torch.zeros(2, 2, 8), pool, torch.zeros(2, 1, dtype=torch.long),
+                                       torch.ones(2, dtype=torch.long), 0)
