@@ -317,6 +317,44 @@ __device__ __forceinline__ float p_pass(uint32_t srow, float scale, float neg_m,
   return ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
 }
 
+// Pass 2 from the S row already in registers (sv, loaded by pass 1): the
+// same probabilities and P stores as p_pass without re-reading TMEM.  Used
+// with 64-key tiles, whose row costs 64 registers.
+template <bool MASK, int kBN>
+__device__ __forceinline__ float p_regs(const float* sv, uint32_t srow, float scale, float neg_m,
+                                        int lim) {
+  const float2 sc2 = make_float2(scale, scale);
+  const float2 nm2 = make_float2(neg_m, neg_m);
+  const float2 one2 = make_float2(1.f, 1.f);
+  float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                  make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int c = 0; c < kBN; c += 32) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const float2 a = ffma2(make_float2(sv[c + e], sv[c + e + 1]), sc2, nm2);
+      float p0, p1;
+      if (kPolyEvery > 0 && (e >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) {
+        const float2 pp = ex2_poly2(a);  // this pair on the FMA pipes
+        p0 = pp.x;
+        p1 = pp.y;
+      } else {
+        p0 = ex2_approx(a.x);
+        p1 = ex2_approx(a.y);
+      }
+      if (MASK) {
+        p0 = c + e <= lim ? p0 : 0.f;
+        p1 = c + e + 1 <= lim ? p1 : 0.f;
+      }
+      rs[(e >> 1) & 3] = ffma2(make_float2(p0, p1), one2, rs[(e >> 1) & 3]);
+      pk[e >> 1] = pack_bf16(p0, p1);
+    }
+    tmem_st16(srow + (c >> 1), pk);
+  }
+  return ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+}
+
 // Shared-memory layout (offsets from a 1024-aligned base).
 template <int D, int kBN>
 struct Smem {
@@ -697,12 +735,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Keys c <= lim of this tile are visible to this row (int32, clamped).
       const int lim = static_cast<int>(max(min(qpos - key0, static_cast<int64_t>(kBN - 1)),
                                            static_cast<int64_t>(-1)));
+      float sv[kBN];  // the S row (kept for pass 2 with 64-key tiles)
       if (warp_live) {
         // Pass 1: row max of the masked raw scores (the scale is positive, so
         // it is applied once to the max).
         float mx;
         {
-          float sv[kBN];  // one TMEM round trip for the whole row
 #pragma unroll
           for (int c = 0; c < kBN; c += 32) tmem_ld32(tmem_s(w, buf) + lane_base + c, sv + c);
           tmem_wait_ld();
@@ -743,8 +781,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // columns already consumed; the masked variant is a separate
         // instantiation so unmasked tiles carry no per-element selects.
         const uint32_t srow = tmem_s(w, buf) + lane_base;
-        const float rsum = need_mask ? p_pass<true, kBN>(srow, p.scale_log2, -m_use, lim)
-                                     : p_pass<false, kBN>(srow, p.scale_log2, -m_use, lim);
+        float rsum;
+        if (kBN == 64)  // the row is still in registers
+          rsum = need_mask ? p_regs<true, kBN>(sv, srow, p.scale_log2, -m_use, lim)
+                           : p_regs<false, kBN>(sv, srow, p.scale_log2, -m_use, lim);
+        else
+          rsum = need_mask ? p_pass<true, kBN>(srow, p.scale_log2, -m_use, lim)
+                           : p_pass<false, kBN>(srow, p.scale_log2, -m_use, lim);
         l = l * alpha + rsum;
         m = m_use;
       }
