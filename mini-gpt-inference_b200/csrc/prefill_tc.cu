@@ -8,23 +8,26 @@
 // tensor core: while one softmax group works on its scores, the MMAs of the
 // other group run.
 //
-// Warp roles (11 warps):
-//   warps 0, 10  TMA producers of K and V: for each 128-key tile they walk
-//            the block table and load, per KV block, boxes {64 d, 1 head,
-//            rbox rows} with 128-byte swizzle into this CTA's K ring (3
-//            stages) and V ring (2 stages); warp 0 also loads the Q tiles.
-//   warp 1   TMEM allocation (512 columns) and the MMA issuer (whole warp,
-//            one elected lane issues):
-//              S_w  = Q_w K^T -> TMEM columns [128w, 128w+128)   (M=128,N=128)
-//              O_w += P_w V   -> TMEM columns [256+128w, +D)     (M=128,N=D)
-//            Q, K and P are K-major SW128 operands; V is read MN-major.
+// Key tiles are BN = 64 (two S buffers per query tile, so S(k+1) is computed
+// while the softmax works on S(k)) or BN = 128 (one S buffer; launches of
+// single-tile chunks, where a CTA's two softmax groups split the keys).
+//
+// Warp roles (12 warps):
+//   warps 0, 10  TMA producers of K and V: for each key tile they walk the
+//            block table and load, per KV block, boxes {64 d, 1 head, rbox
+//            rows} with 128-byte swizzle into this CTA's K ring and V ring;
+//            warp 0 also loads the Q tiles.
+//   warp 1   TMEM allocation (512 columns) and the S issuer (whole warp, one
+//            elected lane issues): S_w = Q_w K^T (M=128, N=BN) into the
+//            group's S buffer; it releases K stages.
+//   warp 11  the P.V issuer: O_w += P_w V (M=128, N=D), P read from TMEM as
+//            the A operand; it releases V stages.  Q, K and P are K-major
+//            SW128 operands; V is read MN-major.
 //   warps 2-5, 6-9  softmax / correction / epilogue of query tile 0 / 1:
-//            thread r of a group owns query row r = TMEM lane r: two passes
-//            over its S row (tcgen05.ld) give the masked row max, then the
-//            probabilities; the running max is kept unless it grows by more
-//            than 2^8 (lazy rescale of O in TMEM); the bf16 P row is written
-//            over the S columns already consumed, and the P.V MMA reads it
-//            from TMEM as its A operand.
+//            thread r of a group owns query row r = TMEM lane r: pass 1
+//            reads its S row and takes the masked max, pass 2 writes the
+//            bf16 probabilities over the S columns; the running max is kept
+//            unless it grows by more than 2^8 (lazy rescale of O in TMEM).
 // V rows beyond the last valid key of the last tile are zeroed in smem
 // before the P.V MMA: unwritten pool rows can hold NaN and 0 * NaN is NaN
 // inside the tensor core as well (minivllm/paged_attention_batch.py:234-240).
