@@ -77,12 +77,15 @@ class DecodeWorkload:
 
     bound, unit = "hbm", "GB/s"
 
-    def __init__(self, name, rank, device, batch=None, ctx=None):
+    def __init__(self, name, rank, device, batch=None, ctx=None, kv_dtype="bf16"):
         self.name, self.device = name, device
+        self.kv_name = kv_dtype
+        self.dt = torch.float32 if kv_dtype == "f32" else torch.bfloat16
+        self.es = 4 if kv_dtype == "f32" else 2
         if name == "cfg4":
             self.B = batch or 64
             lens = [ctx or 32768] * self.B
-            self.desc = (f"config 4: long-context split-K decode, bf16 KV, {self.B} requests/GPU"
+            self.desc = (f"config 4: long-context split-K decode, {kv_dtype} KV, {self.B} requests/GPU"
                          f" x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
         else:
             self.B = batch or 256
@@ -91,27 +94,27 @@ class DecodeWorkload:
             lens[0] = 1
             if lens[-1] % S == 0:
                 lens[-1] -= 1
-            self.desc = (f"config 3: ragged decode, bf16 KV, batch {self.B}/GPU, contexts"
+            self.desc = (f"config 3: ragged decode, {kv_dtype} KV, batch {self.B}/GPU, contexts"
                          " ~U[1,4096], H=32, D=128, S=16, fused KV write")
         self.lens = lens
         counts = [math.ceil(n / S) for n in lens]
         P = sum(counts) + max(1, sum(counts) // 100)
         g = torch.Generator(device=device).manual_seed(20260000 + rank)
-        self.k = torch.empty((1, P, S, H, D), dtype=torch.bfloat16, device=device).normal_(generator=g)
+        self.k = torch.empty((1, P, S, H, D), dtype=self.dt, device=device).normal_(generator=g)
         self.v = torch.empty_like(self.k).normal_(generator=g)
         tables = _tables(counts, torch.randperm(P, generator=g, device=device).cpu())
         slots = [int(tables[b, (n - 1) // S]) * S + (n - 1) % S for b, n in enumerate(lens)]
         hg = torch.Generator().manual_seed(rank)
         self.host = {
-            "q": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
-            "k_new": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
-            "v_new": torch.randn((self.B, H, D), generator=hg).to(torch.bfloat16).pin_memory(),
+            "q": torch.randn((self.B, H, D), generator=hg).to(self.dt).pin_memory(),
+            "k_new": torch.randn((self.B, H, D), generator=hg).to(self.dt).pin_memory(),
+            "v_new": torch.randn((self.B, H, D), generator=hg).to(self.dt).pin_memory(),
             "tables": tables.pin_memory(),
             "ctx": torch.tensor(lens, dtype=torch.int64).pin_memory(),
             "slots": torch.tensor(slots, dtype=torch.int64).pin_memory(),
         }
         self.dev = {k: v.to(device) for k, v in self.host.items()}
-        self.out_h = torch.empty((self.B, H, D), dtype=torch.bfloat16).pin_memory()
+        self.out_h = torch.empty((self.B, H, D), dtype=self.dt).pin_memory()
         self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
         self.kv_gb = 2 * self.k.numel() * self.k.element_size() / 1e9
 
@@ -123,7 +126,7 @@ class DecodeWorkload:
 
     def prepare(self):
         self.call = self._call(self.dev, prepare=True,
-                               out=torch.empty((self.B, H, D), dtype=torch.bfloat16,
+                               out=torch.empty((self.B, H, D), dtype=self.dt,
                                                device=self.device))
 
     def step(self):
@@ -135,8 +138,8 @@ class DecodeWorkload:
 
     def work(self) -> float:  # algorithmic bytes per step
         from b200attn import decode_bytes
-        return decode_bytes(self.lens, H, D, S, kv_bytes=2, q_bytes=2, out_bytes=2, idx_bytes=8,
-                            fused_in_bytes=2)
+        return decode_bytes(self.lens, H, D, S, kv_bytes=self.es, q_bytes=self.es,
+                            out_bytes=self.es, idx_bytes=8, fused_in_bytes=self.es)
 
     def h2d_bytes(self):
         return sum(t.numel() * t.element_size() for t in self.host.values())
@@ -147,8 +150,8 @@ class DecodeWorkload:
     def config(self, world):
         return {"workload": self.desc, "batch_per_gpu": self.B, "global_batch": self.B * world,
                 "context_lens": str(self.lens[0]) if self.name == "cfg4" else "U[1,4096]",
-                "heads": H, "head_dim": D, "block_size": S, "kv_dtype": "bf16",
-                "q_dtype": "bf16", "accumulate": "f32", "fused_kv_write": True,
+                "heads": H, "head_dim": D, "block_size": S, "kv_dtype": self.kv_name,
+                "q_dtype": self.kv_name, "accumulate": "f32", "fused_kv_write": True,
                 "l2": "inputs larger than L2 (KV pool %.1f GB per GPU), no flush" % self.kv_gb,
                 "parallelism": f"request-sharded dp{world} (no data-path collective)"}
 
@@ -285,7 +288,7 @@ class ScatterWorkload:
 
 def make_workload(name, rank, device, args):
     if name in ("cfg4", "cfg3"):
-        return DecodeWorkload(name, rank, device, args.batch, args.ctx)
+        return DecodeWorkload(name, rank, device, args.batch, args.ctx, args.kv_dtype)
     if name == "cfg5-t512":
         return PrefillWorkload(512, rank, device)
     if name == "cfg5-t64":
@@ -567,7 +570,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "metric": metric, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic", "config": wl.config(world),
+            "dtype": getattr(wl, "kv_name", "bf16"), "data": "synthetic", "config": wl.config(world),
             **wl.extra(ms_max, world, args.steps),
             "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
                          "frac": achieved / peak, "peak_source": src,
@@ -597,6 +600,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="decode requests per GPU (default: the workload's; smaller for profiling)")
+    ap.add_argument("--kv-dtype", choices=("bf16", "f32"), default="bf16",
+                    help="KV pool dtype of the decode workloads (configuration 3 is specified for both)")
     ap.add_argument("--ctx", type=int, default=None,
                     help="context length of cfg4 requests (default 32768)")
     args = ap.parse_args()
