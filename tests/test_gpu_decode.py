@@ -238,3 +238,35 @@ def test_large_context_split_k_sampled():
                                          torch.arange(counts[b])[None], lens[b:b + 1], 0,
                                          compute_dtype=torch.float64).float()
         assert (out[b:b + 1].cpu() - want).abs().max().item() <= BF16_ATOL
+
+
+def test_very_long_context_split_k():
+    """A 256k-token context (the split-K plan at its 64-split cap, a 16384-wide
+    table) and a 100k one, bf16 KV, checked against the float64 oracle on
+    each sequence's compacted sub-pool."""
+    d = _dev()
+    g = torch.Generator(device=d).manual_seed(11)
+    B, H, D, S = 2, 2, 128, 16
+    lens = torch.tensor([262144, 100000])
+    counts = [math.ceil(int(n) / S) for n in lens]
+    P = sum(counts) + 5
+    k = torch.randn((1, P, S, H, D), generator=g, device=d).to(torch.bfloat16)
+    v = torch.randn((1, P, S, H, D), generator=g, device=d).to(torch.bfloat16)
+    perm = torch.randperm(P, generator=g, device=d).cpu()
+    tables = torch.full((B, max(counts)), -1, dtype=torch.int64)
+    nxt = 0
+    for b, c in enumerate(counts):
+        tables[b, :c] = perm[nxt:nxt + c]
+        nxt += c
+    q = torch.randn((B, H, D), generator=g, device=d)
+    pool = cases.Pool(k, v, S)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    out = _decode(q, pool, tables.to(d), lens.to(d), 0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for b in range(B):
+        phys = tables[b, :counts[b]].to(d)
+        want = oracle.paged_decode_dense(q[b:b + 1].cpu(), k[:, phys].cpu().float(),
+                                         v[:, phys].cpu().float(), torch.arange(counts[b])[None],
+                                         lens[b:b + 1], 0, compute_dtype=torch.float64).float()
+        assert (out[b:b + 1].cpu() - want).abs().max().item() <= BF16_ATOL
