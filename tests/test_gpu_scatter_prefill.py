@@ -216,3 +216,27 @@ def test_prefill_batch_mixed_chunk_lengths_against_oracle():
         for o, want in zip(outs, wants):
             err = (o.float().cpu() - want).abs().max().item()
             assert err <= 2e-2, f"max abs {err:.3e}"
+
+
+@pytest.mark.parametrize("prefix,T", [(32768, 300), (32768, 64)])
+def test_prefill_long_prefix(prefix, T):
+    """A 32k-token prefix: hundreds of key tiles streamed through one CTA's
+    rings (64-key double-buffered tiles for T=300, 128-key key-split tiles
+    for T=64), against the float64 oracle."""
+    from b200attn import chunked_prefill_b200, kv_scatter_b200
+
+    c = cases.prefill_case(prefix, T, 2, 128, 16, 31 + T, dtype=torch.bfloat16, n_layer=1,
+                           layer_idx=0)
+    d = _dev()
+    pool = c.pool.to(d)
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    kv_scatter_b200(c.k.to(d), c.v.to(d), pool, c.slots, 0)
+    out = chunked_prefill_b200(c.q.to(d), pool, c.block_table, prefix, 0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    oracle.kv_scatter(kp, vp, c.k, c.v, c.slots, 0)
+    want = oracle.prefix_prefill_from_pool(c.q.float(), kp.float(), vp.float(), c.block_table,
+                                           prefix, 0, compute_dtype=torch.float64).float()
+    err = (out.float().cpu() - want).abs().max().item()
+    assert err <= 2e-2, f"max abs {err:.3e}"
