@@ -1,7 +1,7 @@
 """Benchmark of the sm_100a paged-attention backend.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg4|cfg3|cfg5-t512|cfg5-t64|scatter]
+                    [--workload cfg4|cfg3|cfg5-t512|cfg5-t64|scatter|qkv-prefill|qkv-decode]
 
 One step = one launch of the hot path over one batch of the workload, with
 inputs resident in HBM (``value``), and the same step through the public
@@ -18,6 +18,11 @@ result copied back, plus a host synchronisation (``e2e``):
   prefill launch over 16 sequences, chunk 512 or 64 tokens, prefixes
   16*U{0..252}; the KV pool is ~2-4 GB (larger than L2).
 * scatter: the slot-mapping KV scatter of 16 x 512 prefill tokens (bf16).
+* qkv-prefill / qkv-decode: the attention's QKV projection with the KV write
+  in its epilogue (tcgen05 GEMM), hidden 4096, over 8192 prefill tokens
+  (TFLOP/s, tensor roofline) or 64 decode tokens (GB/s, HBM roofline: the
+  100 MB weight read dominates); the line also carries the unfused sequence
+  (cuBLAS matmul, then the scatter) timed in the same run.
 
 Under torchrun (N>1) each rank runs its shard on its own GPU; the only
 collective is the all-reduce(MAX) of the timings.  Rank 0 prints one JSON
@@ -286,6 +291,102 @@ class ScatterWorkload:
         return {}
 
 
+class QkvWorkload:
+    """The attention's QKV projection with the KV write in its epilogue
+    (b200_qkv_kv_write), bf16, hidden 4096 (H=32, D=128): a prefill batch
+    of 16 x 512 tokens (tensor-bound) or a decode batch of 64 tokens
+    (bound by the 100 MB weight read)."""
+
+    def __init__(self, name, rank, device):
+        self.name, self.device = name, device
+        self.T = 16 * 512 if name == "qkv-prefill" else 64
+        self.C = H * D
+        self.bound, self.unit = ("tensor", "TFLOP/s") if name == "qkv-prefill" else ("hbm", "GB/s")
+        T, C = self.T, self.C
+        g = torch.Generator().manual_seed(rank)
+        gd = torch.Generator(device=device).manual_seed(40260000 + rank)
+        P = T // S * 2
+        self.k = torch.zeros((1, P, S, H, D), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
+        self.w = (torch.empty((3 * C, C), dtype=torch.bfloat16, device=device)
+                  .normal_(0.0, 0.02, generator=gd))
+        self.x_h = torch.randn((T, C), generator=g).to(torch.bfloat16).pin_memory()
+        self.slots_h = torch.randperm(P * S, generator=g)[:T].pin_memory()
+        self.x, self.slots = self.x_h.to(device), self.slots_h.to(device)
+        self.q_h = torch.empty((T, C), dtype=torch.bfloat16).pin_memory()
+        self.desc = (f"fused QKV projection + KV write (tcgen05), bf16, {T} tokens, hidden {C}"
+                     f" (H=32, D=128), weight [3C, C], S=16")
+
+    def prepare(self):
+        from b200attn import qkv_kv_write_b200
+        self.call = qkv_kv_write_b200(self.x, self.w, self.pool, self.slots, 0, prepare=True)
+
+    def step(self):
+        self.call()
+
+    def e2e_step(self):
+        from b200attn import qkv_kv_write_b200
+        q = qkv_kv_write_b200(self.x_h.to(self.device, non_blocking=True), self.w, self.pool,
+                              self.slots_h.to(self.device, non_blocking=True), 0)
+        self.q_h.copy_(q.view(self.T, self.C), non_blocking=True)
+
+    def flops(self) -> float:
+        return 2.0 * self.T * self.C * 3 * self.C
+
+    def bytes(self) -> float:
+        T, C = self.T, self.C
+        return 2.0 * (3 * C * C + T * C + T * 3 * C) + 8 * T
+
+    def work(self) -> float:
+        return self.flops() if self.bound == "tensor" else self.bytes()
+
+    def h2d_bytes(self):
+        return self.x_h.numel() * 2 + self.slots_h.numel() * 8
+
+    def d2h_bytes(self):
+        return self.q_h.numel() * 2
+
+    def config(self, world):
+        return {"workload": self.desc, "tokens_per_gpu": self.T, "hidden": self.C, "heads": H,
+                "head_dim": D, "block_size": S, "accumulate": "f32",
+                "l2": "weights %.0f MB, no flush between steps" % (3 * self.C * self.C * 2 / 1e6),
+                "parallelism": f"token-sharded dp{world}"}
+
+    def extra(self, ms_max, world, steps):
+        """The unfused sequence the kernel replaces, timed the same way:
+        torch's bf16 matmul (cuBLAS) into a [T, 3C] tensor, then the
+        slot-mapping scatter of its k and v thirds."""
+        from b200attn import kv_scatter_b200
+        T, C = self.T, self.C
+        y = torch.empty((T, 3 * C), dtype=torch.bfloat16, device=self.device)
+
+        def unfused(scatter):
+            torch.matmul(self.x, self.w.t(), out=y)
+            if scatter:
+                kv_scatter_b200(y[:, C:2 * C].view(T, H, D), y[:, 2 * C:].view(T, H, D),
+                                self.pool, self.slots, 0)
+
+        res = {}
+        with torch.inference_mode():
+            for scatter in (False, True):
+                for _ in range(3):
+                    unfused(scatter)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    unfused(scatter)
+                e1.record()
+                torch.cuda.synchronize(self.device)
+                ms = e0.elapsed_time(e1) / steps
+                key = "cublas_matmul_plus_scatter" if scatter else "cublas_matmul_alone"
+                res[key] = {"ms_per_step": ms,
+                            "value": self.work() / (ms * 1e-3) / (1e12 if self.bound == "tensor" else 1e9),
+                            "unit": self.unit}
+        res["fused_ms_per_step"] = ms_max / steps
+        return {"unfused_comparison": res}
+
+
 def make_workload(name, rank, device, args):
     if name in ("cfg4", "cfg3"):
         return DecodeWorkload(name, rank, device, args.batch, args.ctx, args.kv_dtype)
@@ -295,6 +396,8 @@ def make_workload(name, rank, device, args):
         return PrefillWorkload(64, rank, device)
     if name == "scatter":
         return ScatterWorkload(rank, device)
+    if name in ("qkv-prefill", "qkv-decode"):
+        return QkvWorkload(name, rank, device)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -447,6 +550,25 @@ def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
         unit = "TFLOP/s"
         sample = (f"2 sequences (prefix 2016 and 1024, chunk {T}), H=32, D=128, fp32, SDPA v2"
                   " prefill restatement (oracle/)")
+    elif workload.startswith("qkv"):
+        # The reference's own CPU path: the qkv Linear (torch, fp32) on a
+        # 256-token sample, chunk(3), then the per-token write loop.
+        n, C = 256, H * D
+        x = torch.randn((n, C), generator=g)
+        w = torch.randn((3 * C, C), generator=g) * 0.02
+        k_pool = torch.zeros((1, n // S * 2, S, H, D))
+        v_pool = torch.zeros_like(k_pool)
+        slots = torch.randperm(k_pool.shape[1] * S, generator=g)[:n].tolist()
+
+        def fn():
+            q, k, v = torch.nn.functional.linear(x, w).chunk(3, dim=-1)
+            oracle.kv_scatter(k_pool, v_pool, k.reshape(n, H, D), v.reshape(n, H, D), slots, 0)
+        if workload == "qkv-prefill":
+            work, unit = 2.0 * n * C * 3 * C, "TFLOP/s"
+        else:
+            work, unit = 4.0 * (3 * C * C + n * C + n * 3 * C), "GB/s"
+        sample = (f"{n} tokens, hidden {C}, fp32 qkv Linear + per-token KVBlockPool.write_layer"
+                  " loop restatement (oracle/)")
     else:
         n = 2048
         k_pool = torch.zeros((1, n // S * 8, S, H, D), dtype=torch.bfloat16)
@@ -470,11 +592,20 @@ def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
             "sample": sample, "seconds_per_step": sec}
 
 
+def metric_name(workload: str, unit: str) -> str:
+    """The metric string of a workload, shared by both arms."""
+    if workload in ("cfg4", "cfg3"):
+        return METRIC
+    what = {"cfg5": "chunked prefill attention", "scatter": "KV scatter",
+            "qkv": "fused QKV projection + KV write"}[workload.split("-")[0]]
+    return f"{workload} {what} {unit}"
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     r = cpu_reference_sample(args.workload, args.steps, args.warmup)
-    line = {"metric": METRIC if args.workload in ("cfg4", "cfg3") else f"{args.workload} {r['unit']}",
+    line = {"metric": metric_name(args.workload, r["unit"]),
             "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -560,12 +691,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         cpu = cpu_reference_sample(args.workload, steps=3, warmup=0)
         cpu.pop("seconds_per_step")
     if rank == 0:
-        if isinstance(wl, DecodeWorkload):
-            metric = METRIC
-        elif isinstance(wl, PrefillWorkload):
-            metric = f"{args.workload} chunked prefill attention {wl.unit}"
-        else:
-            metric = f"{args.workload} KV scatter {wl.unit}"
+        metric = metric_name(args.workload, wl.unit)
         line = {
             "metric": metric, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
@@ -596,7 +722,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="cfg4",
-                    choices=("cfg4", "cfg3", "cfg5-t512", "cfg5-t64", "scatter"))
+                    choices=("cfg4", "cfg3", "cfg5-t512", "cfg5-t64", "scatter", "qkv-prefill",
+                             "qkv-decode"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="decode requests per GPU (default: the workload's; smaller for profiling)")

@@ -229,6 +229,40 @@ B200_API int b200_chunked_prefill_batch(const b200_prefill_batch_args_t* args, v
 #define B200_NO_ALLOC_SCRATCH_BYTES (4u << 20)
 B200_API int b200_paged_decode_no_alloc(const b200_decode_args_t* args, void* stream);
 
+/*
+ * Fused QKV projection with the KV write in its epilogue (bf16, tcgen05):
+ *   y[t, :] = x[t, :] . W^T           W: [3C, C] weight of the bias-free
+ *                                     `qkv` Linear (minivllm/attention.py:79-83)
+ *   q_out[t, :] = y[t, 0:C]
+ *   pool.k[layer, slot[t] / S, slot[t] % S, :, :] = y[t, C:2C]   (H * D = C)
+ *   pool.v[layer, slot[t] / S, slot[t] % S, :, :] = y[t, 2C:3C]
+ * with f32 accumulation and one round-to-nearest-even bf16 rounding per
+ * output.  Replaces the projection, chunk(3) split and KV write of
+ * forward_prefill_chunk (minivllm/attention.py:177-208, through
+ * KVBlockPool.write_layer, minivllm/kv_block_pool.py:91-109) and of
+ * forward_decode_batch (minivllm/attention.py:360-392); the attention call
+ * that follows reads k/v from the pool (decode without k_new).
+ * A slot outside [0, P*S) skips that token's k/v and sets B200_DEV_BAD_SLOT
+ * in *status; its q row is still written.
+ */
+typedef struct {
+  b200_kv_pool_t pool;              /* bf16, num_heads * head_dim == hidden */
+  int64_t layer_idx;
+  int64_t num_tokens;               /* T (0 is a no-op)                     */
+  int64_t hidden;                   /* C: a multiple of 64                  */
+  const void* x;                    /* [T, C] bf16, unit inner stride       */
+  int64_t x_row_stride;             /* elements, a multiple of 8            */
+  const void* weight;               /* [3C, C] bf16, contiguous             */
+  void* q_out;                      /* [T, C] bf16, unit inner stride       */
+  int64_t q_row_stride;             /* elements, a multiple of 8            */
+  const void* slot_mapping;         /* device [T]                           */
+  int64_t slot_stride;
+  b200_index_t slot_dtype;
+  int32_t* status;                  /* optional device word (may be NULL)   */
+} b200_qkv_kv_write_args_t;
+
+B200_API int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* stream);
+
 /* Workspace bytes the decode launch needs for these sizes. */
 B200_API size_t b200_paged_decode_workspace_size(int64_t batch, int64_t num_heads,
                                         int64_t head_dim, int64_t table_width,

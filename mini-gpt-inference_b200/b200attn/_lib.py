@@ -72,6 +72,13 @@ class PrefillArgs(ctypes.Structure):
                 ("workspace", _p), ("workspace_bytes", ctypes.c_size_t), ("status", _p)]
 
 
+class QkvKvWriteArgs(ctypes.Structure):
+    _fields_ = [("pool", KVPool), ("layer_idx", _i64), ("num_tokens", _i64), ("hidden", _i64),
+                ("x", _p), ("x_row_stride", _i64), ("weight", _p), ("q_out", _p),
+                ("q_row_stride", _i64), ("slot_mapping", _p), ("slot_stride", _i64),
+                ("slot_dtype", ctypes.c_int), ("status", _p)]
+
+
 class PrefillBatchArgs(ctypes.Structure):
     _fields_ = [("num_seqs", _i64), ("seqs", ctypes.POINTER(PrefillArgs))]
 
@@ -83,6 +90,7 @@ SIGNATURES = {
     "b200_chunked_prefill": (ctypes.c_int, [ctypes.POINTER(PrefillArgs), _p]),
     "b200_chunked_prefill_batch": (ctypes.c_int, [ctypes.POINTER(PrefillBatchArgs), _p]),
     "b200_paged_decode_no_alloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _p]),
+    "b200_qkv_kv_write": (ctypes.c_int, [ctypes.POINTER(QkvKvWriteArgs), _p]),
     "b200_paged_decode_workspace_size": (
         ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int32]),
     "b200_chunked_prefill_workspace_size": (

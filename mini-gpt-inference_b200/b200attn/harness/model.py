@@ -7,7 +7,8 @@ MiniGPT.prefill_chunk / decode_batch (model.py:189-248) and the pre-LN
 TransformerBlock (block.py:47-93).  Attention goes through a backend object;
 the default, B200Backend, is the fused KV-write + paged decode kernel and
 the scatter + prefix-aware prefill kernels -- the "sm100" branches of
-INTEGRATION.md's host diff.
+the reference-side host diff.  B200FusedQKVBackend (bf16 models) also moves
+the QKV projection and the KV write into one tcgen05 GEMM.
 """
 from __future__ import annotations
 
@@ -36,6 +37,30 @@ class B200Backend:
         return chunked_prefill_b200(q, pool, block_table, start_pos, layer_idx)
 
 
+class B200FusedQKVBackend(B200Backend):
+    """B200Backend with the QKV projection and the KV write fused into one
+    tcgen05 GEMM (b200_qkv_kv_write): the k and v thirds of the projection
+    go from the GEMM epilogue straight into the pool, and attention then
+    reads them from there.  Needs bf16 weights and a bf16 KV pool."""
+
+    fused_qkv = True
+
+    def decode_fused(self, x: Tensor, weight: Tensor, pool: KVBlockPool,
+                     metadata: DecodeBatchMetadata, layer_idx: int) -> Tensor:
+        from ..ops import paged_attention_batch_b200, qkv_kv_write_b200
+
+        q = qkv_kv_write_b200(x, weight, pool, metadata.slot_mapping, layer_idx)
+        return paged_attention_batch_b200(q, pool, metadata.block_tables,
+                                          metadata.context_lengths, layer_idx)
+
+    def prefill_fused(self, x: Tensor, weight: Tensor, pool: KVBlockPool, block_table: Tensor,
+                      start_pos: int, slot_mapping: Tensor, layer_idx: int) -> Tensor:
+        from ..ops import chunked_prefill_b200, qkv_kv_write_b200
+
+        q = qkv_kv_write_b200(x, weight, pool, slot_mapping, layer_idx)
+        return chunked_prefill_b200(q, pool, block_table, start_pos, layer_idx)
+
+
 class Attention(nn.Module):
     def __init__(self, n_embd: int, n_head: int):
         super().__init__()
@@ -56,16 +81,23 @@ class Attention(nn.Module):
                              layer_idx: int, backend) -> Tensor:
         B, T, C = x.shape
         assert T == 1
-        q, k, v = self._split(x, B)
-        out = backend.decode(q, k, v, pool, metadata, layer_idx)
+        if getattr(backend, "fused_qkv", False):
+            out = backend.decode_fused(x.reshape(B, C), self.qkv.weight, pool, metadata, layer_idx)
+        else:
+            q, k, v = self._split(x, B)
+            out = backend.decode(q, k, v, pool, metadata, layer_idx)
         return self.project(out.reshape(B, 1, C))
 
     def forward_prefill_chunk(self, x: Tensor, ctx: "PrefillChunk", backend) -> Tensor:
         B, T, C = x.shape
         assert B == 1
-        q, k, v = self._split(x, T)
-        out = backend.prefill(q, k, v, ctx.pool, ctx.block_table, ctx.start_pos,
-                              ctx.slot_mapping, ctx.layer_idx)
+        if getattr(backend, "fused_qkv", False):
+            out = backend.prefill_fused(x.reshape(T, C), self.qkv.weight, ctx.pool, ctx.block_table,
+                                        ctx.start_pos, ctx.slot_mapping, ctx.layer_idx)
+        else:
+            q, k, v = self._split(x, T)
+            out = backend.prefill(q, k, v, ctx.pool, ctx.block_table, ctx.start_pos,
+                                  ctx.slot_mapping, ctx.layer_idx)
         return self.project(out.reshape(1, T, C))
 
 

@@ -10,6 +10,10 @@ These are drop-ins for the attention backends of minivllm
   decode KV write of minivllm/attention.py:370-392.
 * :func:`kv_scatter_b200` replaces the KV writes of attention.py:370-392 and
   the per-token ``KVBlockPool.write_layer`` loop of attention.py:193-208.
+* :func:`qkv_kv_write_b200` is the attention's QKV projection (the
+  bias-free ``qkv`` Linear, attention.py:79-83) with the KV write of
+  attention.py:193-208 / :370-392 in the GEMM epilogue: it returns q and
+  leaves k and v in the pool.
 * :func:`chunked_prefill_b200` replaces the prefill attention branches of
   ``forward_prefill_chunk`` (attention.py:215-299): first-chunk SDPA, the
   prefix-aware SDPA v2 and the per-token reference.
@@ -280,6 +284,74 @@ def kv_scatter_b200(k: torch.Tensor, v: torch.Tensor, pool, slot_mapping,
         args.status = status.data_ptr()
     call = PreparedCall(lib.b200_kv_scatter, args, dev, None, "kv scatter",
                         (k, v, pool.k, pool.v, slots, status))
+    return call if prepare else call()
+
+
+def qkv_kv_write_b200(x: torch.Tensor, weight: torch.Tensor, pool, slot_mapping,
+                      layer_idx: int, *, q_out: torch.Tensor | None = None,
+                      status: torch.Tensor | None = None, prepare: bool = False):
+    """q = (x W^T)[:, :C] as [T, H, D]; k and v go straight into the pool.
+
+    Same result as the reference's ``q, k, v = self.qkv(x).chunk(3, -1)``
+    followed by the KV write at ``slot_mapping`` (attention.py:177-208,
+    :360-392), computed as one tcgen05 GEMM whose epilogue stores the k and
+    v thirds of each output row at the token's slot.
+
+    x: [T, C] bf16 (rows 16-byte aligned, unit inner stride); weight: the
+    [3C, C] bf16 ``qkv.weight``; pool: a bf16 KVBlockPool with H * D = C;
+    slot_mapping: [T] integer CUDA tensor or host ints.  Returns q_out
+    ([T, C] bf16, allocated when not given) viewed as [T, H, D].
+    """
+    _inference_only(x, weight)
+    lib = _lib.load()
+    if not x.is_cuda:
+        raise ValueError("CUDA x required for the b200 backend")
+    if x.ndim != 2 or weight.ndim != 2:
+        raise ValueError("x must be [T, C] and weight [3C, C]")
+    t, c = x.shape
+    if weight.shape != (3 * c, c):
+        raise ValueError(f"weight must have shape [3C, C] = [{3 * c}, {c}]")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("x and weight must be bfloat16")
+    if x.stride(1) != 1 or not weight.is_contiguous():
+        raise ValueError("x rows and weight must be contiguous")
+    pstruct = _pool_struct(pool)
+    if pool.k.dtype != torch.bfloat16:
+        raise ValueError("the fused QKV projection needs a bfloat16 KV pool")
+    h, d = pool.k.shape[3:]
+    if h * d != c:
+        raise ValueError("pool num_heads * head_dim must equal the hidden size")
+    if not (0 <= layer_idx < pool.k.shape[0]):
+        raise ValueError("layer_idx outside KV pool")
+    dev = x.device
+    if any(z.device != dev for z in (weight, pool.k, pool.v)):
+        raise ValueError("all inputs must reside on same CUDA device")
+    slots = _index_tensor(slot_mapping, dev, "slot_mapping")
+    if slots.shape != (t,):
+        raise ValueError("slot_mapping must have shape [T]")
+    if q_out is None:
+        q_out = torch.empty((t, c), dtype=torch.bfloat16, device=dev)
+    elif (q_out.shape != (t, c) or q_out.dtype != torch.bfloat16 or q_out.device != dev
+          or q_out.stride(1) != 1):
+        raise ValueError("q_out must be a [T, C] bfloat16 tensor with contiguous rows")
+    args = _lib.QkvKvWriteArgs()
+    args.pool = pstruct
+    args.layer_idx = layer_idx
+    args.num_tokens = t
+    args.hidden = c
+    args.x = x.data_ptr()
+    args.x_row_stride = x.stride(0) if t > 1 else c
+    args.weight = weight.data_ptr()
+    args.q_out = q_out.data_ptr()
+    args.q_row_stride = q_out.stride(0) if t > 1 else c
+    args.slot_mapping = slots.data_ptr()
+    args.slot_stride = slots.stride(0) if t > 0 else 1
+    args.slot_dtype = _INDEX[slots.dtype]
+    if status is not None:
+        args.status = status.data_ptr()
+    q = q_out.view(t, h, d)
+    call = PreparedCall(lib.b200_qkv_kv_write, args, dev, q, "qkv projection",
+                        (x, weight, pool.k, pool.v, slots, q_out, status))
     return call if prepare else call()
 
 

@@ -13,13 +13,17 @@ C-ABI entry points as :mod:`b200attn.ops`.
     b200attn::chunked_prefill(Tensor q, Tensor k, Tensor v, Tensor(a!) k_pool,
                               Tensor(b!) v_pool, Tensor block_table, Tensor slot_mapping,
                               int prefix_len, int layer_idx) -> Tensor
+    b200attn::qkv_kv_write(Tensor x, Tensor weight, Tensor(a!) k_pool, Tensor(b!) v_pool,
+                           Tensor slot_mapping, int layer_idx) -> Tensor
 
 The pools are the KVBlockPool tensors ``[L, P, S, H, D]`` (S = block size).
 ``paged_decode`` writes k_new/v_new into the pools when they are given
 (minivllm/attention.py:370-392). ``chunked_prefill`` scatters the chunk's k/v
 at ``slot_mapping`` (attention.py:193-208) and returns the prefix-aware
-attention of the chunk (attention.py:215-299). Importing this module registers
-the ops.
+attention of the chunk (attention.py:215-299). ``qkv_kv_write`` is the bf16
+QKV projection (attention.py:79-83) that stores k and v at ``slot_mapping``
+from its epilogue and returns q as [T, H, D] (attention.py:177-208,
+:360-392). Importing this module registers the ops.
 """
 from __future__ import annotations
 
@@ -30,7 +34,7 @@ import torch
 
 from . import ops
 
-__all__ = ["paged_decode", "kv_scatter", "chunked_prefill"]
+__all__ = ["paged_decode", "kv_scatter", "chunked_prefill", "qkv_kv_write"]
 
 
 def _pool(k_pool: torch.Tensor, v_pool: torch.Tensor) -> SimpleNamespace:
@@ -78,3 +82,17 @@ def chunked_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_pool: t
 @chunked_prefill.register_fake
 def _(q, k, v, k_pool, v_pool, block_table, slot_mapping, prefix_len, layer_idx):
     return torch.empty_like(q, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("b200attn::qkv_kv_write", mutates_args=("k_pool", "v_pool"))
+def qkv_kv_write(x: torch.Tensor, weight: torch.Tensor, k_pool: torch.Tensor,
+                 v_pool: torch.Tensor, slot_mapping: torch.Tensor, layer_idx: int) -> torch.Tensor:
+    q = x.new_empty((x.shape[0], k_pool.shape[3], k_pool.shape[4]))
+    ops.qkv_kv_write_b200(x, weight, _pool(k_pool, v_pool), slot_mapping, layer_idx,
+                          q_out=q.view(x.shape[0], -1))
+    return q
+
+
+@qkv_kv_write.register_fake
+def _(x, weight, k_pool, v_pool, slot_mapping, layer_idx):
+    return x.new_empty((x.shape[0], k_pool.shape[3], k_pool.shape[4]))

@@ -23,7 +23,7 @@ LIB_NAME = "libb200attn.so"
 BUILD_DIR = PKG_ROOT / "_build"
 
 SOURCES = ["host_util.cu", "capi.cu", "kv_scatter.cu", "paged_decode.cu", "paged_decode_no_alloc.cu",
-           "prefill_tc.cu", "selftest.cu"]
+           "prefill_tc.cu", "qkv_proj.cu", "selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

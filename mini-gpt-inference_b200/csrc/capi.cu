@@ -179,6 +179,36 @@ int b200_kv_scatter(const b200_kv_scatter_args_t* args, void* stream) {
   return launch_kv_scatter(a, static_cast<cudaStream_t>(stream));
 }
 
+int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* stream) {
+  clear_error();
+  if (args == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null arguments");
+  const b200_qkv_kv_write_args_t& a = *args;
+  int rc = check_pool(a.pool, a.layer_idx);
+  if (rc != B200_OK) return rc;
+  if (a.num_tokens < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
+  if (a.num_tokens == 0) return B200_OK;
+  B200_CHECK(a.x != nullptr && a.weight != nullptr && a.q_out != nullptr && a.slot_mapping != nullptr,
+             B200_ERR_INVALID_ARGUMENT, "x, weight, q_out and slot_mapping must be non-null");
+  B200_CHECK(a.pool.dtype == B200_DTYPE_BF16, B200_ERR_UNSUPPORTED,
+             "qkv projection: the KV pool must be bfloat16");
+  B200_CHECK(a.hidden >= 64 && a.hidden % 64 == 0, B200_ERR_UNSUPPORTED,
+             "qkv projection: hidden size must be a positive multiple of 64");
+  B200_CHECK(a.pool.num_heads * a.pool.head_dim == a.hidden, B200_ERR_INVALID_ARGUMENT,
+             "qkv projection: num_heads * head_dim must equal the hidden size");
+  B200_CHECK(a.hidden <= (int64_t(1) << 20) && a.num_tokens < (int64_t(1) << 31) / 2,
+             B200_ERR_UNSUPPORTED, "qkv projection: sizes too large");
+  B200_CHECK(a.x_row_stride >= a.hidden && a.x_row_stride % 8 == 0 &&
+                 a.q_row_stride >= a.hidden && a.q_row_stride % 8 == 0,
+             B200_ERR_UNSUPPORTED,
+             "qkv projection: x and q_out rows must be 16-byte aligned and not overlap");
+  B200_CHECK(reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(a.weight) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(a.q_out) % 16 == 0,
+             B200_ERR_UNSUPPORTED, "qkv projection: x, weight and q_out must be 16-byte aligned");
+  B200_CHECK(valid_index(a.slot_dtype), B200_ERR_INVALID_ARGUMENT, "slot_mapping must be integer");
+  return launch_qkv_kv_write(a, static_cast<cudaStream_t>(stream));
+}
+
 int b200_paged_decode(const b200_decode_args_t* args, void* stream) {
   clear_error();
   if (args == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null arguments");

@@ -1,0 +1,391 @@
+// qkv_proj.cu -- the attention's fused QKV projection with the KV-cache write
+// in its epilogue, on tcgen05 tensor cores (bf16 operands, f32 accumulate).
+//
+//   y = x W^T            x [T, C], W [3C, C]: the bias-free `qkv` Linear of
+//                        minivllm/attention.py:79-83
+//   q_out[t]                    = y[t, 0:C]
+//   pool.k[layer, slot[t] / S, slot[t] % S] = y[t, C:2C]
+//   pool.v[layer, slot[t] / S, slot[t] % S] = y[t, 2C:3C]
+//
+// The reference computes qkv(x), splits it with chunk(3) and views
+// (attention.py:177-191, :360-368), then writes k and v into the pool per
+// token (attention.py:193-208 through KVBlockPool.write_layer) or by
+// index_put (attention.py:370-392).  A pool row (one token of one block, all
+// heads) is H * D = C contiguous elements, exactly the k (or v) third of an
+// output row, so the epilogue stores each 32-column run of a row straight
+// into the row's slot and k and v never exist as a separate tensor.
+//
+// Persistent CTAs (one per SM) walk the output tiles (128 tokens x BN
+// features), token tile fastest, so the CTAs running at once share their
+// weight tiles in L2.  Warp roles (6 warps):
+//   warp 0     TMA producer: the x tile (128 x 64) and the W tile (BN x 64)
+//              of each k-step, 128-byte swizzle, into a STAGES-deep ring;
+//   warp 1     TMEM allocation and MMA issue: D[acc] += A B^T with M = 128,
+//              N = BN, K = 16 per instruction (both operands K-major); two
+//              TMEM accumulators, so the epilogue of one tile overlaps the
+//              MMAs of the next;
+//   warps 2-5  epilogue: thread r owns output row r (TMEM lane r), reads 32
+//              columns at a time, rounds to bf16 (nearest even) and stores
+//              the 64-byte run to q_out or to the row's pool slot.
+// Rows past T and columns past 3C are zero-filled by TMA and not stored.
+// A slot outside [0, P*S) sets B200_DEV_BAD_SLOT and skips that row's k and
+// v (q is still written).  Every mbarrier wait is bounded; on a timeout the
+// CTA reports B200_DEV_WAIT_TIMEOUT, lets its own copies and MMAs finish,
+// frees TMEM and exits.
+#include <string.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "host_util.h"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kBM = 128;                 // tokens per tile (TMEM lanes)
+constexpr int kBK = 64;                  // reduction elements per stage (one 128-byte row)
+constexpr int kThreads = 192;            // producer, MMA issuer, 4 epilogue warps
+constexpr int kRingBytes = 192 * 1024;   // operand ring (1 CTA per SM)
+
+template <int BN>
+struct QkvCfg {
+  static constexpr int A_BYTES = kBM * 128;  // x tile: 128 rows of 64 bf16
+  static constexpr int B_BYTES = BN * 128;   // W tile: BN rows of 64 bf16
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = kRingBytes / STAGE;  // 4 / 6 / 8 for BN 256 / 128 / 64
+  static constexpr int BAR = STAGES * STAGE;
+  static constexpr int BYTES = BAR + 256;
+  static constexpr int TMEM_COLS = 2 * BN;  // two f32 accumulators
+  static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area too small");
+};
+
+struct QkvParams {
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  const void* slots;
+  int64_t q_rs;     // q_out row stride (elements)
+  int64_t ss;       // slot stride (elements)
+  int64_t T, C;
+  int64_t row0;     // layer * P * S: the layer's first pool row
+  int64_t nslots;   // P * S
+  int32_t slots_i64;
+  int32_t m_tiles, n_tiles, k_iters;
+  int32_t* status;
+};
+
+// Stores 32 f32 values as 32 bf16 (64 contiguous bytes, 16-byte aligned).
+__device__ __forceinline__ void store_run32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    d[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                      pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    qkv_kv_write_kernel(const __grid_constant__ CUtensorMap tmx,
+                        const __grid_constant__ CUtensorMap tmw, const QkvParams p) {
+  using Cfg = QkvCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR);  // [STAGES] operands landed
+  uint64_t* empty = full + STAGES;                                // [STAGES] MMAs read them
+  uint64_t* acc_full = empty + STAGES;                            // [2] accumulator complete
+  uint64_t* acc_empty = acc_full + 2;                             // [2] epilogue drained it
+  uint64_t* drain = acc_empty + 2;                                // all MMAs done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  volatile int32_t* abort_v = abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ntiles = p.m_tiles * p.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      int64_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+        const int m0 = (t % p.m_tiles) * kBM;
+        const int n0 = (t / p.m_tiles) * BN;
+        for (int kb = 0; kb < p.k_iters; ++kb) {
+          const int st = static_cast<int>(issued % STAGES);
+          const uint32_t use = static_cast<uint32_t>(issued / STAGES);
+          if (*abort_v || !mbar_wait(&empty[st], (use & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(Cfg::STAGE));
+          uint8_t* a = smem + st * Cfg::STAGE;
+          tma_load_2d(a, &tmx, &full[st], kb * kBK, m0);
+          tma_load_2d(a + Cfg::A_BYTES, &tmw, &full[st], kb * kBK, n0);
+          ++issued;
+        }
+      }
+      if (!ok) {
+        report(p.status, B200_DEV_WAIT_TIMEOUT);
+        *abort_v = 1;
+      }
+      // Each of the last (up to) STAGES loads must land before the CTA
+      // exits; earlier ones were waited for before their stage was reused.
+      for (int64_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+        if (!mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u)) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          break;
+        }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // The whole warp runs the loop (values stay warp-uniform); every lane
+    // waits on the barriers and a vote makes the outcome uniform;
+    // elect.sync picks the issuing lane.
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(bar, parity)) != 0;
+    };
+    constexpr uint32_t idesc = idesc_bf16(kBM, BN, false);
+    // Stage bases are 1024-aligned; a k-step of 16 elements is 32 bytes
+    // inside the 128-byte swizzle row (+2 in the descriptor's address
+    // field, which cannot carry: shared memory is < 256 KB).
+    const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
+    int64_t consumed = 0;
+    bool ok = true;
+    int i = 0;
+    for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      if (!wait_all(&acc_empty[acc], (use & 1u) ^ 1u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t td = tmem + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < p.k_iters; ++kb, ++consumed) {
+        const int st = static_cast<int>(consumed % STAGES);
+        if (!wait_all(&full[st], static_cast<uint32_t>(consumed / STAGES) & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = da0 + static_cast<uint64_t>((st * Cfg::STAGE) >> 4);
+        const uint64_t db = da + static_cast<uint64_t>(Cfg::A_BYTES >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          mma_bf16(td, da + static_cast<uint64_t>(kk * 2), db + static_cast<uint64_t>(kk * 2), idesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+      }
+      if (!ok) break;
+      mma_commit(&acc_full[acc]);
+    }
+    if (!ok && lane == 0) {
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+      *abort_v = 1;
+    }
+    // Every MMA this thread issued completes before TMEM is freed.
+    mma_commit(drain);
+    if (!__all_sync(0xffffffffu, mbar_wait(drain, 0)) && lane == 0)
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // A warp may only touch TMEM lanes [32 * (warp % 4), +32): warps 2-5
+    // cover quarters 2, 3, 0, 1.
+    const int qd = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
+        if (lane == 0) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          *abort_v = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(t % p.m_tiles) * kBM + qd * 32 + lane;
+      const int64_t n0 = static_cast<int64_t>(t / p.m_tiles) * BN;
+      const bool live = row < p.T;
+      // The slot is needed only when the tile reaches the k / v columns.
+      int64_t dst_row = -1;
+      if (live && n0 + BN > p.C) {
+        const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
+        if (slot >= 0 && slot < p.nslots) {
+          dst_row = (p.row0 + slot) * p.C;
+        } else {
+          report(p.status, B200_DEV_BAD_SLOT);
+        }
+      }
+      const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        __syncwarp();  // tcgen05.ld is warp-collective
+        tmem_ld32(tacc + static_cast<uint32_t>(c), v);
+        tmem_wait_ld();
+        const int64_t n = n0 + c;
+        if (live && n < 3 * p.C) {
+          if (n < p.C) {
+            store_run32(p.q_out + row * p.q_rs + n, v);
+          } else if (dst_row >= 0) {
+            // C is a multiple of 64, so a 32-column run never straddles thirds.
+            if (n < 2 * p.C)
+              store_run32(p.k_pool + dst_row + (n - p.C), v);
+            else
+              store_run32(p.v_pool + dst_row + (n - 2 * p.C), v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Tensor-core clocks of one M128 x N x K16 bf16 MMA (measured on B200:
+// N=64 is shared-memory-bound at 48, N=128 takes 64, N=256 takes 128).
+int mma_clocks(int bn) { return bn == 64 ? 48 : bn == 128 ? 64 : 128; }
+
+template <int BN>
+int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const DeviceInfo& dev) {
+  using Cfg = QkvCfg<BN>;
+  const int64_t T = a.num_tokens, C = a.hidden;
+  const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
+  if (smem > static_cast<size_t>(dev.max_smem_optin))
+    return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
+
+  CUtensorMap tx, tw;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
+    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
+                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(BN)};
+    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               const_cast<void*>(a.weight), dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  static int configured[64] = {0};
+  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+    cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write)");
+    configured[dev.device] = 1;
+  }
+  QkvParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
+  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
+  prm.slots = a.slot_mapping;
+  prm.q_rs = a.q_row_stride;
+  prm.ss = a.slot_stride;
+  prm.T = T;
+  prm.C = C;
+  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
+  prm.nslots = a.pool.num_blocks * a.pool.block_size;
+  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
+  prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
+  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, BN));
+  prm.k_iters = static_cast<int32_t>(C / kBK);
+  prm.status = a.status;
+  const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.num_sms));
+  qkv_kv_write_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "qkv_kv_write launch");
+  return B200_OK;
+}
+
+}  // namespace
+
+int qkv_pick_bn(int64_t T, int64_t C, int num_sms) {
+  const int64_t m_tiles = ceil_div(T, kBM);
+  const int cand[3] = {256, 128, 64};
+  if (m_tiles <= 2) {
+    // Few tokens (decode): the weights dominate and are read once; the
+    // widest tile that still gives every SM a tile streams them fastest.
+    for (int bn : cand)
+      if (m_tiles * ceil_div(3 * C, bn) >= num_sms) return bn;
+    return 64;
+  }
+  // Otherwise: fewest tensor clocks per SM, counting the partial last wave;
+  // ties go to the wider tile (less operand traffic per flop).
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int bn : cand) {
+    const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
+    const int64_t cost = ceil_div(tiles, num_sms) * mma_clocks(bn);
+    if (best_cost < 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream) {
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != B200_OK) return rc;
+  switch (qkv_pick_bn(a.num_tokens, a.hidden, dev.num_sms)) {
+    case 256:
+      return launch_bn<256>(a, stream, dev);
+    case 128:
+      return launch_bn<128>(a, stream, dev);
+    default:
+      return launch_bn<64>(a, stream, dev);
+  }
+}
+
+}  // namespace b200

@@ -15,11 +15,13 @@ def prompts() -> list[list[int]]:
     return [torch.randint(0, CFG2["vocab"], (p,), generator=g).tolist() for p in CFG2["prompts"]]
 
 
-def run_cfg2(run_name: str, device: str, backend=None, mode: str = "eager"):
+def run_cfg2(run_name: str, device: str, backend=None, mode: str = "eager",
+             dtype: torch.dtype = torch.float32):
     """Runs configuration 2 through the harness; returns (tokens, counts, runtime).
 
     mode: "eager" (host-built metadata per step), "device_tables" (persistent
-    device block tables) or "graphs" (device tables + CUDA-graph decode)."""
+    device block tables) or "graphs" (device tables + CUDA-graph decode).
+    dtype: weights and KV pool (the configuration is specified in fp32)."""
     if mode not in ("eager", "device_tables", "graphs"):
         raise ValueError(mode)
     from b200attn.harness import MiniGPT, SequenceState, build_runtime, init_weights
@@ -27,12 +29,12 @@ def run_cfg2(run_name: str, device: str, backend=None, mode: str = "eager"):
     model = MiniGPT(n_embd=CFG2["n_embd"], n_head=CFG2["n_head"], vocab_size=CFG2["vocab"],
                     block_size=CFG2["pos"], n_layer=CFG2["n_layer"], backend=backend).eval()
     init_weights(model, seed=0)
-    model.to(device)
+    model.to(device=device, dtype=dtype)
     run = CFG2["runs"][run_name]
     rt = build_runtime(model, num_blocks=run["num_blocks"], block_size=CFG2["block_size"],
                        max_running=CFG2["max_running"], token_budget=CFG2["token_budget"],
                        policy=run["policy"], n_head=CFG2["n_head"],
-                       head_dim=CFG2["n_embd"] // CFG2["n_head"],
+                       head_dim=CFG2["n_embd"] // CFG2["n_head"], kv_dtype=dtype,
                        device_tables=mode != "eager", graphs=mode == "graphs")
     rt.runner.kv_pool.k.fill_(float("nan"))  # unwritten KV must never be read
     rt.runner.kv_pool.v.fill_(float("nan"))

@@ -47,6 +47,45 @@ def test_ctypes_struct_sizes_match_c_layout():
     assert ctypes.sizeof(_lib.KVPool) == 64
     assert ctypes.sizeof(_lib.ScatterArgs) == 64 + 8 * 4 + 48 + 8 + 8 + 8 + 8 + 8
     assert ctypes.sizeof(_lib.PrefillBatchArgs) == 16
+    assert ctypes.sizeof(_lib.QkvKvWriteArgs) == 64 + 10 * 8 + 8 + 8
+
+
+def test_qkv_kv_write_rejects_bad_arguments_without_gpu():
+    """Host validation of the fused QKV projection runs before any CUDA call."""
+    from b200attn import _lib
+
+    lib = _lib.load()
+
+    def args(**kw):
+        a = _lib.QkvKvWriteArgs()
+        a.pool = _lib.KVPool(1 << 20, 2 << 20, 2, 8, 16, 4, 64, _lib.DTYPE_BF16)
+        a.layer_idx, a.num_tokens, a.hidden = 1, 5, 256
+        a.x, a.x_row_stride, a.weight = 3 << 20, 256, 4 << 20
+        a.q_out, a.q_row_stride, a.slot_mapping = 5 << 20, 256, 6 << 20
+        a.slot_stride, a.slot_dtype = 1, _lib.INDEX_I64
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return ctypes.byref(a)
+
+    import ctypes
+
+    bad = {
+        "hidden not a multiple of 64": dict(hidden=96),
+        "heads x head_dim != hidden": dict(hidden=192),
+        "x rows not 16-byte aligned": dict(x_row_stride=260),
+        "q rows overlap": dict(q_row_stride=128),
+        "x misaligned": dict(x=(3 << 20) + 8),
+        "null weight": dict(weight=None),
+        "f32 pool": dict(pool=_lib.KVPool(1 << 20, 2 << 20, 2, 8, 16, 4, 64, _lib.DTYPE_F32)),
+        "layer outside pool": dict(layer_idx=2),
+        "bad slot dtype": dict(slot_dtype=7),
+    }
+    for why, kw in bad.items():
+        rc = lib.b200_qkv_kv_write(args(**kw), None)
+        assert rc in (_lib.ERR_INVALID_ARGUMENT, _lib.ERR_UNSUPPORTED), why
+    assert lib.b200_qkv_kv_write(None, None) == _lib.ERR_INVALID_ARGUMENT
+    # Zero tokens is a no-op that succeeds without touching the device.
+    assert lib.b200_qkv_kv_write(args(num_tokens=0), None) == _lib.OK
 
 
 def test_last_error_and_invalid_arguments_without_gpu():

@@ -1,0 +1,168 @@
+"""Fused QKV projection + KV write (b200_qkv_kv_write) on the GPU, through the C ABI.
+
+The reference computes ``q, k, v = self.qkv(x).chunk(3, -1)`` and writes k and
+v at each token's slot (minivllm/attention.py:177-208, :360-392).  The kernel
+is a bf16 tcgen05 GEMM with f32 accumulation and one bf16 rounding per
+output, so it is checked against the same product in fp32 (torch, on the
+upcast bf16 operands): every output must be the fp32 value rounded to bf16
+up to the accumulation order, i.e. |got - ref| <= 2^-8 |ref| + 1e-4 (unit
+roundoff of bf16 plus f32 summation-order slack).  Pool rows that no slot
+names must keep their bits (the pool is NaN-poisoned first).
+"""
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+BF16_U = 2.0 ** -8
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def _make(T, C, H, S, L, layer, seed, slot_dtype=torch.int64, x_pad=0, P=None):
+    g = torch.Generator().manual_seed(seed)
+    D = C // H
+    need = -(-T // S) + 2
+    P = P or max(need * 2, 4)
+    x_full = torch.randn(T, C + x_pad, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3 * C, C, generator=g) / C ** 0.5).to(torch.bfloat16)
+    slots = torch.randperm(P * S, generator=g)[:T].to(slot_dtype)
+    d = _dev()
+    pool = SimpleNamespace(
+        k=torch.full((L, P, S, H, D), float("nan"), dtype=torch.bfloat16, device=d),
+        v=torch.full((L, P, S, H, D), float("nan"), dtype=torch.bfloat16, device=d),
+        block_size=S)
+    x = x_full.to(d)[:, :C]
+    return SimpleNamespace(x=x, w=w.to(d), slots=slots.to(d), pool=pool, T=T, C=C, H=H, D=D,
+                           S=S, L=L, P=P, layer=layer)
+
+
+def _ref(c):
+    return c.x.float() @ c.w.float().t()  # [T, 3C] in fp32 (products of bf16 are exact)
+
+
+def _assert_rounded(got, ref, what):
+    err = (got.float() - ref).abs()
+    bound = ref.abs() * BF16_U + 1e-4
+    bad = (err > bound).sum().item()
+    assert bad == 0, f"{what}: {bad} elements beyond bf16 rounding, max err {err.max().item():.3e}"
+
+
+def _check_pool(c, y, status_bits=0):
+    """k/v rows at the slots equal y's thirds; every other row is untouched."""
+    C = c.C
+    kf = c.pool.k.view(c.L, c.P * c.S, C)
+    vf = c.pool.v.view(c.L, c.P * c.S, C)
+    slots = c.slots.long()
+    valid = (slots >= 0) & (slots < c.P * c.S)
+    rows = slots[valid]
+    _assert_rounded(kf[c.layer, rows], y[valid, C:2 * C], "k rows")
+    _assert_rounded(vf[c.layer, rows], y[valid, 2 * C:], "v rows")
+    written = torch.zeros(c.L, c.P * c.S, dtype=torch.bool, device=kf.device)
+    written[c.layer, rows] = True
+    assert torch.isnan(kf[~written].float()).all() and torch.isnan(vf[~written].float()).all()
+
+
+@pytest.mark.parametrize("T,C,H,S,L,layer", [
+    (1, 256, 8, 16, 2, 1),       # one decode token, cfg2-sized model (H=8, D=32)
+    (5, 256, 8, 16, 1, 0),
+    (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (64-wide output tiles)
+    (129, 4096, 32, 16, 2, 1),   # two token tiles, the second ragged (128-wide tiles)
+    (300, 512, 4, 16, 1, 0),
+    (1000, 4096, 32, 16, 1, 0),  # prefill chunk (256-wide tiles)
+    (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step
+    (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
+    (200, 3136, 49, 16, 1, 0),   # 128-wide tiles, 3C = 73.5 tiles: ragged last output tile
+    (1000, 4160, 65, 16, 1, 0),  # 256-wide tiles, 3C = 48.75 tiles: ragged last output tile
+])
+def test_qkv_kv_write_matches_fp32_projection(T, C, H, S, L, layer):
+    from b200attn import qkv_kv_write_b200
+
+    c = _make(T, C, H, S, L, layer, seed=T * 7 + C)
+    status = torch.zeros(1, dtype=torch.int32, device=_dev())
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, layer, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert q.shape == (T, H, C // H) and q.dtype == torch.bfloat16
+    y = _ref(c)
+    _assert_rounded(q.reshape(T, C), y[:, :C], "q")
+    _check_pool(c, y)
+
+
+def test_qkv_kv_write_agrees_with_cublas_within_one_ulp():
+    """Against torch's bf16 matmul (cuBLAS, f32 accumulation, one rounding):
+    the two differ only where the f32 sums straddle a bf16 rounding point."""
+    from b200attn import qkv_kv_write_b200
+
+    c = _make(512, 4096, 32, 16, 1, 0, seed=3)
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, 0)
+        y = c.x @ c.w.t()
+    torch.cuda.synchronize()
+    diff = (q.reshape(512, 4096).float() - y[:, :4096].float()).abs()
+    assert (diff <= y[:, :4096].float().abs() * 2 * BF16_U + 1e-4).all()
+    same = (q.reshape(512, 4096) == y[:, :4096]).float().mean().item()
+    assert same > 0.95, f"only {same:.3f} of q equals cuBLAS bit for bit"
+
+
+def test_qkv_kv_write_strided_x_int32_slots():
+    from b200attn import qkv_kv_write_b200
+
+    c = _make(150, 512, 8, 16, 1, 0, seed=11, slot_dtype=torch.int32, x_pad=64)
+    assert c.x.stride(0) == 576
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, 0)
+    torch.cuda.synchronize()
+    y = _ref(c)
+    _assert_rounded(q.reshape(150, 512), y[:, :512], "q")
+    _check_pool(c, y)
+
+
+def test_qkv_kv_write_bad_slots_are_flagged_and_skipped():
+    from b200attn import _lib, qkv_kv_write_b200
+
+    c = _make(40, 256, 8, 16, 1, 0, seed=5)
+    c.slots[3] = -1
+    c.slots[17] = c.P * c.S  # one past the pool
+    status = torch.zeros(1, dtype=torch.int32, device=_dev())
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, 0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & _lib.DEV_BAD_SLOT
+    y = _ref(c)
+    _assert_rounded(q.reshape(40, 256), y[:, :256], "q (all rows, bad slots included)")
+    _check_pool(c, y)
+
+
+def test_qkv_kv_write_q_out_buffer_and_prepared_call():
+    from b200attn import qkv_kv_write_b200
+
+    c = _make(33, 256, 8, 16, 1, 0, seed=9)
+    q_out = torch.empty(33, 256, dtype=torch.bfloat16, device=_dev())
+    with torch.inference_mode():
+        call = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, 0, q_out=q_out, prepare=True)
+        q1 = call()
+        q1c = q1.clone()
+        q2 = call()
+    torch.cuda.synchronize()
+    assert q1.data_ptr() == q_out.data_ptr() and torch.equal(q2, q1c)
+    _assert_rounded(q_out, _ref(c)[:, :256], "q")
+
+
+def test_torch_op_qkv_kv_write():
+    import b200attn  # noqa: F401  (registers torch.ops.b200attn.*)
+
+    c = _make(20, 256, 8, 16, 1, 0, seed=21)
+    with torch.inference_mode():
+        q = torch.ops.b200attn.qkv_kv_write(c.x, c.w, c.pool.k, c.pool.v, c.slots, 0)
+    torch.cuda.synchronize()
+    y = _ref(c)
+    _assert_rounded(q.reshape(20, 256), y[:, :256], "q")
+    _check_pool(c, y)

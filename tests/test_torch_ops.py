@@ -9,11 +9,12 @@ def test_ops_registered_with_schemas():
     import b200attn  # noqa: F401  (registers the ops)
 
     sch = {n: str(getattr(torch.ops.b200attn, n).default._schema)
-           for n in ("paged_decode", "kv_scatter", "chunked_prefill")}
+           for n in ("paged_decode", "kv_scatter", "chunked_prefill", "qkv_kv_write")}
     assert "Tensor(a1!) k_pool, Tensor(a2!) v_pool" in sch["paged_decode"]
     assert sch["paged_decode"].endswith("Tensor? slot_mapping=None) -> Tensor")
     assert sch["kv_scatter"].endswith("SymInt layer_idx) -> ()")
     assert "Tensor slot_mapping, SymInt prefix_len, SymInt layer_idx) -> Tensor" in sch["chunked_prefill"]
+    assert "Tensor(a2!) k_pool, Tensor(a3!) v_pool, Tensor slot_mapping, SymInt layer_idx) -> Tensor" in sch["qkv_kv_write"]
 
 
 def test_fake_implementations_give_output_shapes():
@@ -34,3 +35,7 @@ def test_fake_implementations_give_output_shapes():
                                                torch.zeros(3, dtype=torch.int64, device="cuda"), sm,
                                                5, 0)
         assert o.shape == (10, 8, 32)
+        x = torch.empty(10, 256, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(768, 256, dtype=torch.bfloat16, device="cuda")
+        q = torch.ops.b200attn.qkv_kv_write(x, w, kp, vp, sm, 0)
+        assert q.shape == (10, 8, 32) and q.dtype == torch.bfloat16
