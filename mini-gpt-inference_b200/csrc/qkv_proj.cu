@@ -284,9 +284,309 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Tensor-core clocks of one M128 x N x K16 bf16 MMA (measured on B200:
-// N=64 is shared-memory-bound at 48, N=128 takes 64, N=256 takes 128).
-int mma_clocks(int bn) { return bn == 64 ? 48 : bn == 128 ? 64 : 128; }
+// ------------------------------------------------------------------ CTA pairs
+// For long token runs the tiles are 256 tokens x 256 features, computed by
+// a cluster of two CTAs with tcgen05.mma.cta_group::2: CTA r of the pair
+// loads token rows [128r, +128) of the x tile and feature rows [128r, +128)
+// of the W tile, and the pair MMA (issued by CTA 0 only) multiplies the
+// pair's 256 x rows by all 256 W rows, each CTA's TMEM receiving the
+// accumulator rows of its own tokens.  Per SM this halves the W bytes
+// staged in shared memory for the same tensor work, which a single CTA
+// with 256-wide tiles is limited by.  Both CTAs' copies complete on CTA 0's
+// stage barrier; CTA 0's MMA commits release the stage in both CTAs and
+// publish each accumulator to both epilogues; each epilogue warp of either
+// CTA returns an accumulator to CTA 0 with one remote arrival.  No copy
+// uses cluster multicast.
+constexpr int kPairBN = 256;
+struct PairCfg {
+  static constexpr int A_BYTES = kBM * 128;        // this CTA's 128 x rows
+  static constexpr int B_BYTES = 128 * 128;        // this CTA's 128 W rows
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = kRingBytes / STAGE;  // 6
+  static constexpr int BAR = STAGES * STAGE;
+  static constexpr int BYTES = BAR + 256;
+  static constexpr int TMEM_COLS = 2 * kPairBN;    // two 256-column accumulators
+  static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area too small");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+  return d;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+
+// 2-D TMA load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair (a shared::cluster address, here CTA 0's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives (once each) on the barrier at this offset in both CTAs of the pair
+// when the MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    qkv_kv_write_pair_kernel(const __grid_constant__ CUtensorMap tmx,
+                             const __grid_constant__ CUtensorMap tmw, const QkvParams p) {
+  using Cfg = PairCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR);  // [STAGES] (CTA 0's are used)
+  uint64_t* empty = full + STAGES;                                // [STAGES] this CTA's stage free
+  uint64_t* acc_full = empty + STAGES;                            // [2] in both CTAs
+  uint64_t* acc_empty = acc_full + 2;                             // [2] (CTA 0's are used)
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  volatile int32_t* abort_v = abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // one arrival per epilogue warp of either CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  // Both CTAs' barriers exist before any copy or commit of the pair targets them.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int m_tiles = static_cast<int>((p.T + 2 * kBM - 1) / (2 * kBM));
+  const int ntiles = m_tiles * p.n_tiles;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      const uint32_t full0 = map_to_rank(full, 0);
+      int64_t issued = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < ntiles; t += npairs) {
+        const int m0 = (t % m_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (t / m_tiles) * kPairBN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < p.k_iters; ++kb) {
+          const int st = static_cast<int>(issued % STAGES);
+          const uint32_t use = static_cast<uint32_t>(issued / STAGES);
+          if (*abort_v || !mbar_wait(&empty[st], (use & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          // CTA 0's stage barrier counts the bytes of both CTAs' copies.
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(2 * Cfg::STAGE));
+          uint8_t* a = smem + st * Cfg::STAGE;
+          const uint32_t bar = full0 + static_cast<uint32_t>(st * 8);
+          tma_load_2d_pair(a, &tmx, bar, kb * kBK, m0);
+          tma_load_2d_pair(a + Cfg::A_BYTES, &tmw, bar, kb * kBK, n0);
+          ++issued;
+        }
+      }
+      if (!ok) {
+        report(p.status, B200_DEV_WAIT_TIMEOUT);
+        *abort_v = 1;
+      }
+      // CTA 0 sees every copy of the pair land on its stage barriers.
+      if (rank == 0)
+        for (int64_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+          if (!mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u)) {
+            report(p.status, B200_DEV_WAIT_TIMEOUT);
+            break;
+          }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (CTA 0)
+    if (rank == 0) {
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(bar, parity)) != 0;
+      };
+      constexpr uint32_t idesc = idesc_bf16(2 * kBM, kPairBN, false);
+      const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
+      int64_t consumed = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = pair; ok && t < ntiles; t += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        if (!wait_all(&acc_empty[acc], (use & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t td = tmem + static_cast<uint32_t>(acc * kPairBN);
+        for (int kb = 0; kb < p.k_iters; ++kb, ++consumed) {
+          const int st = static_cast<int>(consumed % STAGES);
+          if (!wait_all(&full[st], static_cast<uint32_t>(consumed / STAGES) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = da0 + static_cast<uint64_t>((st * Cfg::STAGE) >> 4);
+          const uint64_t db = da + static_cast<uint64_t>(Cfg::A_BYTES >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_pair(td, da + static_cast<uint64_t>(kk * 2), db + static_cast<uint64_t>(kk * 2),
+                          idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit_pair_both(&empty[st]);
+        }
+        if (!ok) break;
+        mma_commit_pair_both(&acc_full[acc]);
+      }
+      if (!ok && lane == 0) {
+        report(p.status, B200_DEV_WAIT_TIMEOUT);
+        *abort_v = 1;
+      }
+      mma_commit_pair_local(drain);
+      if (!__all_sync(0xffffffffu, mbar_wait(drain, 0)) && lane == 0)
+        report(p.status, B200_DEV_WAIT_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int qd = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const uint32_t acc_empty0 = map_to_rank(acc_empty, 0);
+    int i = 0;
+    for (int t = pair; t < ntiles; t += npairs, ++i) {
+      const int acc = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
+        if (lane == 0) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          *abort_v = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(t % m_tiles) * 2 * kBM + rank * kBM + qd * 32 + lane;
+      const int64_t n0 = static_cast<int64_t>(t / m_tiles) * kPairBN;
+      const bool live = row < p.T;
+      int64_t dst_row = -1;
+      if (live && n0 + kPairBN > p.C) {
+        const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
+        if (slot >= 0 && slot < p.nslots) {
+          dst_row = (p.row0 + slot) * p.C;
+        } else {
+          report(p.status, B200_DEV_BAD_SLOT);
+        }
+      }
+      const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * kPairBN);
+#pragma unroll 1
+      for (int c = 0; c < kPairBN; c += 32) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tacc + static_cast<uint32_t>(c), v);
+        tmem_wait_ld();
+        const int64_t n = n0 + c;
+        if (live && n < 3 * p.C) {
+          if (n < p.C) {
+            store_run32(p.q_out + row * p.q_rs + n, v);
+          } else if (dst_row >= 0) {
+            if (n < 2 * p.C)
+              store_run32(p.k_pool + dst_row + (n - p.C), v);
+            else
+              store_run32(p.v_pool + dst_row + (n - 2 * p.C), v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty0 + static_cast<uint32_t>(acc * 8));
+    }
+  }
+  // Neither CTA frees TMEM or exits while the pair's MMAs, copies or
+  // arrivals may still touch it (every wait above is bounded, so both CTAs
+  // get here).
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Shared-memory clocks per 16-deep k-step on one SM: the MMA reads the A
+// and B rows of the step and TMA writes the same bytes into the ring, at
+// 128 bytes per clock between them (above the tensor clocks for every
+// single-CTA tile width: M128 x N takes N/2 clocks).  A CTA pair with
+// 256-wide tiles stages 128 A rows and 128 B rows per SM: 128 clocks, equal
+// to its tensor clocks.
+int step_clocks(int bn) { return (kBM + bn) / 2; }
+constexpr int kPairStepClocks = 128;
 
 template <int BN>
 int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const DeviceInfo& dev) {
@@ -347,6 +647,77 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
   return B200_OK;
 }
 
+int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const DeviceInfo& dev) {
+  using Cfg = PairCfg;
+  const int64_t T = a.num_tokens, C = a.hidden;
+  const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
+  if (smem > static_cast<size_t>(dev.max_smem_optin))
+    return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
+  CUtensorMap tx, tw;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
+    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
+                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), 128u};
+    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               const_cast<void*>(a.weight), dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  static int max_pairs[64] = {0};
+  int pairs = dev.num_sms / 2;
+  if (dev.device >= 0 && dev.device < 64) {
+    if (max_pairs[dev.device] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_pair_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_pair)");
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(dev.num_sms & ~1), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_pair_kernel, &cfg);
+      if (e != cudaSuccess || n < 1) {
+        (void)cudaGetLastError();
+        n = dev.num_sms / 2;
+      }
+      max_pairs[dev.device] = n;
+    }
+    pairs = max_pairs[dev.device];
+  }
+  QkvParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
+  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
+  prm.slots = a.slot_mapping;
+  prm.q_rs = a.q_row_stride;
+  prm.ss = a.slot_stride;
+  prm.T = T;
+  prm.C = C;
+  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
+  prm.nslots = a.pool.num_blocks * a.pool.block_size;
+  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
+  prm.m_tiles = static_cast<int32_t>(ceil_div(T, 2 * kBM));
+  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, kPairBN));
+  prm.k_iters = static_cast<int32_t>(C / kBK);
+  prm.status = a.status;
+  const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
+  const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, pairs));
+  qkv_kv_write_pair_kernel<<<grid, kThreads, smem, stream>>>(tx, tw, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "qkv_kv_write_pair launch");
+  return B200_OK;
+}
+
 }  // namespace
 
 int qkv_pick_bn(int64_t T, int64_t C, int num_sms) {
@@ -359,14 +730,15 @@ int qkv_pick_bn(int64_t T, int64_t C, int num_sms) {
       if (m_tiles * ceil_div(3 * C, bn) >= num_sms) return bn;
     return 64;
   }
-  // Otherwise: fewest tensor clocks per SM, counting the partial last wave;
-  // ties go to the wider tile (less operand traffic per flop).
-  int best = 256;
-  int64_t best_cost = -1;
+  // Otherwise: fewest shared-memory-bound clocks per SM, counting the
+  // partial last wave; 0 selects the CTA-pair kernel (256 x 256 tiles).
+  int best = 0;
+  int64_t best_cost = ceil_div(ceil_div(T, 2 * kBM) * ceil_div(3 * C, kPairBN), num_sms / 2) *
+                      kPairStepClocks;
   for (int bn : cand) {
     const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
-    const int64_t cost = ceil_div(tiles, num_sms) * mma_clocks(bn);
-    if (best_cost < 0 || cost < best_cost) {
+    const int64_t cost = ceil_div(tiles, num_sms) * step_clocks(bn);
+    if (cost < best_cost) {
       best = bn;
       best_cost = cost;
     }
@@ -379,6 +751,8 @@ int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream) 
   int rc = current_device_info(&dev);
   if (rc != B200_OK) return rc;
   switch (qkv_pick_bn(a.num_tokens, a.hidden, dev.num_sms)) {
+    case 0:
+      return launch_pair(a, stream, dev);
     case 256:
       return launch_bn<256>(a, stream, dev);
     case 128:

@@ -75,11 +75,12 @@ def _check_pool(c, y, status_bits=0):
     (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (64-wide output tiles)
     (129, 4096, 32, 16, 2, 1),   # two token tiles, the second ragged (128-wide tiles)
     (300, 512, 4, 16, 1, 0),
-    (1000, 4096, 32, 16, 1, 0),  # prefill chunk (256-wide tiles)
+    (1000, 4096, 32, 16, 1, 0),  # prefill chunk (CTA pairs, 256 x 256 tiles)
+    (600, 2048, 16, 16, 2, 1),   # CTA pairs; the second CTA of the last pair has no rows
     (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step
     (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
     (200, 3136, 49, 16, 1, 0),   # 128-wide tiles, 3C = 73.5 tiles: ragged last output tile
-    (1000, 4160, 65, 16, 1, 0),  # 256-wide tiles, 3C = 48.75 tiles: ragged last output tile
+    (1000, 4160, 65, 16, 1, 0),  # CTA pairs, 3C = 48.75 tiles: ragged last output tile
 ])
 def test_qkv_kv_write_matches_fp32_projection(T, C, H, S, L, layer):
     from b200attn import qkv_kv_write_b200
