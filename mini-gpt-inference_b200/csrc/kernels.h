@@ -17,10 +17,16 @@ int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream);
 int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream);
 bool prefill_tc_supported(const b200_prefill_args_t& a);
 // One warp waiting on an mbarrier nothing arrives on, with the given limit.
-// Fused QKV projection + KV write (tcgen05, bf16); qkv_pick_bn is the
-// output-tile width it launches with for T tokens of hidden size C.
+// Fused QKV projection + KV write (tcgen05, bf16).  qkv_plan is the kernel
+// and tile shape it launches for T tokens of hidden size C: single CTAs with
+// BN-wide tiles, CTA pairs with 256 x 256 tiles, or split-K clusters.
+struct QkvPlan {
+  enum Kind { kSingle = 0, kPair = 1, kSplit = 2 };
+  int kind;
+  int bn;
+  int splits;
+};
 int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream);
-int qkv_pick_bn(int64_t T, int64_t C, int num_sms);
 int launch_bounded_wait_selftest(int32_t* status, int64_t limit_ns, cudaStream_t stream);
 
 // Split-K planning shared by the launcher and the workspace query.

@@ -16,8 +16,7 @@
 // into the row's slot and k and v never exist as a separate tensor.
 //
 // Persistent CTAs (one per SM) walk the output tiles (128 tokens x BN
-// features), token tile fastest, so the CTAs running at once share their
-// weight tiles in L2.  Warp roles (6 warps):
+// features) in the grouped order of tile_coords.  Warp roles (6 warps):
 //   warp 0     TMA producer: the x tile (128 x 64) and the W tile (BN x 64)
 //              of each k-step, 128-byte swizzle, into a STAGES-deep ring;
 //   warp 1     TMEM allocation and MMA issue: D[acc] += A B^T with M = 128,
@@ -76,6 +75,22 @@ struct QkvParams {
   int32_t m_tiles, n_tiles, k_iters;
   int32_t* status;
 };
+
+// Tile order: token tiles run fastest inside groups covering kGroupRows
+// tokens, and a group sweeps every weight tile before the next group
+// starts, so the CTAs running at once share a few MB of x and of W in L2
+// (the 126 MB L2 holds neither all of x nor all of W at prefill sizes).
+constexpr int kGroupRows = 4096;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group, int& mt,
+                                            int& nt) {
+  const int per_group = group * n_tiles;
+  const int g = t / per_group;
+  const int first = g * group;
+  const int rows = min(group, m_tiles - first);
+  const int r = t - g * per_group;
+  mt = first + r % rows;
+  nt = r / rows;
+}
 
 // Stores 32 f32 values as 32 bf16 (64 contiguous bytes, 16-byte aligned).
 __device__ __forceinline__ void store_run32(__nv_bfloat16* dst, const float* v) {
@@ -140,8 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
-        const int m0 = (t % p.m_tiles) * kBM;
-        const int n0 = (t / p.m_tiles) * BN;
+        int mt, nt;
+        tile_coords(t, p.m_tiles, p.n_tiles, kGroupRows / kBM, mt, nt);
+        const int m0 = mt * kBM;
+        const int n0 = nt * BN;
         for (int kb = 0; kb < p.k_iters; ++kb) {
           const int st = static_cast<int>(issued % STAGES);
           const uint32_t use = static_cast<uint32_t>(issued / STAGES);
@@ -237,8 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(t % p.m_tiles) * kBM + qd * 32 + lane;
-      const int64_t n0 = static_cast<int64_t>(t / p.m_tiles) * BN;
+      int mt, nt;
+      tile_coords(t, p.m_tiles, p.n_tiles, kGroupRows / kBM, mt, nt);
+      const int64_t row = static_cast<int64_t>(mt) * kBM + qd * 32 + lane;
+      const int64_t n0 = static_cast<int64_t>(nt) * BN;
       const bool live = row < p.T;
       // The slot is needed only when the tile reaches the k / v columns.
       int64_t dst_row = -1;
@@ -436,8 +455,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int t = pair; ok && t < ntiles; t += npairs) {
-        const int m0 = (t % m_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = (t / m_tiles) * kPairBN + static_cast<int>(rank) * 128;
+        int mt, nt;
+        tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
+        const int m0 = mt * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = nt * kPairBN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < p.k_iters; ++kb) {
           const int st = static_cast<int>(issued % STAGES);
           const uint32_t use = static_cast<uint32_t>(issued / STAGES);
@@ -529,8 +550,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(t % m_tiles) * 2 * kBM + rank * kBM + qd * 32 + lane;
-      const int64_t n0 = static_cast<int64_t>(t / m_tiles) * kPairBN;
+      int mt, nt;
+      tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
+      const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + qd * 32 + lane;
+      const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
       const bool live = row < p.T;
       int64_t dst_row = -1;
       if (live && n0 + kPairBN > p.C) {
@@ -575,6 +598,210 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(Cfg::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ split K
+// Few tokens (decode): reading the 3C x C weight dominates, and one
+// 256-wide tile per CTA would keep only 3C / 256 SMs streaming it (48 at
+// C = 4096).  The reduction is split instead: a cluster of `splits` CTAs
+// computes one output tile, CTA r accumulating k-steps [r * kpb, +kpb) in
+// its own TMEM.  Each CTA stages its partial rows (live tokens only) in its
+// shared memory; CTA r then sums tokens r, r + splits, ... over the
+// cluster's staging areas in rank order (the same order every run), rounds
+// once to bf16 and stores them, 64 threads per token row.
+constexpr int kSplitBN = 256;
+constexpr int kStageRowWords = kSplitBN + 4;  // padded: 16-byte stores of a warp hit distinct banks
+using SplitCfg = QkvCfg<kSplitBN>;
+static_assert(kBM * kStageRowWords * 4 <= SplitCfg::BAR, "staging must fit in the operand ring");
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
+  int32_t v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    qkv_kv_write_split_kernel(const __grid_constant__ CUtensorMap tmx,
+                              const __grid_constant__ CUtensorMap tmw, const QkvParams p,
+                              int splits, int kpb) {
+  using Cfg = SplitCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  volatile int32_t* abort_v = abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kSplitBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int tile = blockIdx.x / splits;
+  const int m0 = (tile % p.m_tiles) * kBM;
+  const int n0 = (tile / p.m_tiles) * kSplitBN;
+  const int k0 = static_cast<int>(rank) * kpb;
+  const int k1 = min(p.k_iters, k0 + kpb);
+  const int live = static_cast<int>(p.T - m0 < kBM ? p.T - m0 : kBM);
+  float* stage_rows = reinterpret_cast<float*>(smem);  // [kBM][kStageRowWords], after the MMAs
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      int issued = 0;
+      for (int kb = k0; kb < k1; ++kb, ++issued) {
+        const int st = issued % STAGES;
+        if (*abort_v || !mbar_wait(&empty[st], ((issued / STAGES) & 1) ^ 1)) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          *abort_v = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(Cfg::STAGE));
+        uint8_t* a = smem + st * Cfg::STAGE;
+        tma_load_2d(a, &tmx, &full[st], kb * kBK, m0);
+        tma_load_2d(a + Cfg::A_BYTES, &tmw, &full[st], kb * kBK, n0);
+      }
+      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+        if (!mbar_wait(&full[j % STAGES], (j / STAGES) & 1)) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          break;
+        }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = idesc_bf16(kBM, kSplitBN, false);
+    const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
+    bool ok = true;
+    for (int kb = k0, j = 0; kb < k1; ++kb, ++j) {
+      const int st = j % STAGES;
+      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&full[st], (j / STAGES) & 1))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t da = da0 + static_cast<uint64_t>((st * Cfg::STAGE) >> 4);
+      const uint64_t db = da + static_cast<uint64_t>(Cfg::A_BYTES >> 4);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk)
+        mma_bf16(tmem, da + static_cast<uint64_t>(kk * 2), db + static_cast<uint64_t>(kk * 2), idesc,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&empty[st]);
+    }
+    if (ok) {
+      mma_commit(acc_full);
+    } else if (lane == 0) {
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+      *abort_v = 1;
+    }
+    mma_commit(drain);
+    if (!__all_sync(0xffffffffu, mbar_wait(drain, 0)) && lane == 0)
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+  } else {
+    // Stage this CTA's partial rows (the operand ring is idle once the
+    // accumulator is complete: every copy was consumed by an MMA before it).
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    if (__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(acc_full, 0))) {
+      tc_fence_after();
+      const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kSplitBN; c += 32) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(trow + static_cast<uint32_t>(c), v);
+        tmem_wait_ld();
+        if (r < live) {
+          float4* dst = reinterpret_cast<float4*>(stage_rows + r * kStageRowWords + c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+      }
+    } else if (lane == 0) {
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+      *abort_v = 1;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_sync_all();  // every partial of the cluster is staged
+  if (warp >= 2) {
+    bool all_ok = true;
+    for (int q = 0; q < splits; ++q)
+      all_ok = all_ok && ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) == 0;
+    if (all_ok) {
+      const int e = threadIdx.x - 64;  // 0..127
+      const int c4 = (e & 63) * 4;      // this thread's 4 columns of a row
+      const int64_t n = n0 + c4;
+      for (int lr = static_cast<int>(rank) + (e >> 6) * splits; lr < live; lr += 2 * splits) {
+        const uint32_t off = smem_u32(stage_rows + lr * kStageRowWords + c4);
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < splits; ++q) {
+          const float4 v = ld_cluster_f4(map_to_rank(stage_rows, static_cast<uint32_t>(q)) +
+                                         (off - smem_u32(stage_rows)));
+          s.x += v.x;
+          s.y += v.y;
+          s.z += v.z;
+          s.w += v.w;
+        }
+        if (n >= 3 * p.C) continue;
+        const int64_t row = m0 + lr;
+        const uint2 w2 = make_uint2(pack_bf16(s.x, s.y), pack_bf16(s.z, s.w));
+        if (n < p.C) {
+          *reinterpret_cast<uint2*>(p.q_out + row * p.q_rs + n) = w2;
+        } else {
+          const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
+          if (slot < 0 || slot >= p.nslots) {
+            report(p.status, B200_DEV_BAD_SLOT);
+          } else if (n < 2 * p.C) {
+            *reinterpret_cast<uint2*>(p.k_pool + (p.row0 + slot) * p.C + (n - p.C)) = w2;
+          } else {
+            *reinterpret_cast<uint2*>(p.v_pool + (p.row0 + slot) * p.C + (n - 2 * p.C)) = w2;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while a peer may still read its staging area
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSplitBN)
                  : "memory");
   }
 }
@@ -718,28 +945,129 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
   return B200_OK;
 }
 
+// Clusters of `cluster` split-K CTAs that can be resident at once (cached).
+int split_capacity(int cluster, size_t smem, const DeviceInfo& dev) {
+  static int cache[64][9] = {};
+  if (dev.device < 0 || dev.device >= 64 || cluster < 2 || cluster > 8) return 0;
+  int& slot = cache[dev.device][cluster];
+  if (slot == 0) {
+    cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_split_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_split)"), 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(cluster * (dev.num_sms / cluster)), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_split_kernel, &cfg);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    slot = n > 0 ? n : -1;
+  }
+  return slot > 0 ? slot : 0;
+}
+
+int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, int splits) {
+  using Cfg = SplitCfg;
+  const int64_t T = a.num_tokens, C = a.hidden;
+  const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
+  CUtensorMap tx, tw;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
+    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
+                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kSplitBN)};
+    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               const_cast<void*>(a.weight), dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != B200_OK) return rc;
+  }
+  QkvParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
+  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
+  prm.slots = a.slot_mapping;
+  prm.q_rs = a.q_row_stride;
+  prm.ss = a.slot_stride;
+  prm.T = T;
+  prm.C = C;
+  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
+  prm.nslots = a.pool.num_blocks * a.pool.block_size;
+  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
+  prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
+  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, kSplitBN));
+  prm.k_iters = static_cast<int32_t>(C / kBK);
+  prm.status = a.status;
+  const int kpb = static_cast<int>(ceil_div(prm.k_iters, splits));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(prm.m_tiles * prm.n_tiles * splits), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qkv_kv_write_split_kernel, tx, tw, prm, splits, kpb);
+  if (e != cudaSuccess) return cuda_fail(e, "qkv_kv_write_split launch");
+  return B200_OK;
+}
+
 }  // namespace
 
-int qkv_pick_bn(int64_t T, int64_t C, int num_sms) {
+QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
+  const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
   const int cand[3] = {256, 128, 64};
   if (m_tiles <= 2) {
-    // Few tokens (decode): the weights dominate and are read once; the
-    // widest tile that still gives every SM a tile streams them fastest.
+    // Few tokens (decode): the weights dominate and are read once.  Split
+    // the reduction over a cluster when that puts more SMs on the weight
+    // stream than one tile per CTA does (every split keeps >= 8 k-steps).
+    const int64_t tiles = m_tiles * ceil_div(3 * C, kSplitBN);
+    const int64_t k_iters = C / kBK;
+    const size_t smem = static_cast<size_t>(SplitCfg::BYTES) + 1024;
+    int best = 1;
+    for (int s = 2; s <= 8; ++s)
+      if (tiles * s <= num_sms && k_iters / s >= 8 && tiles <= split_capacity(s, smem, dev))
+        best = s;
+    if (best >= 2) return {QkvPlan::kSplit, kSplitBN, best};
+    // Otherwise the widest tile that still gives every SM a tile.
     for (int bn : cand)
-      if (m_tiles * ceil_div(3 * C, bn) >= num_sms) return bn;
-    return 64;
+      if (m_tiles * ceil_div(3 * C, bn) >= num_sms) return {QkvPlan::kSingle, bn, 1};
+    return {QkvPlan::kSingle, 64, 1};
   }
   // Otherwise: fewest shared-memory-bound clocks per SM, counting the
-  // partial last wave; 0 selects the CTA-pair kernel (256 x 256 tiles).
-  int best = 0;
+  // partial last wave; CTA pairs (256 x 256 tiles) unless a single-CTA
+  // tile width is cheaper.
+  QkvPlan best{QkvPlan::kPair, kPairBN, 1};
   int64_t best_cost = ceil_div(ceil_div(T, 2 * kBM) * ceil_div(3 * C, kPairBN), num_sms / 2) *
                       kPairStepClocks;
   for (int bn : cand) {
     const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
     const int64_t cost = ceil_div(tiles, num_sms) * step_clocks(bn);
     if (cost < best_cost) {
-      best = bn;
+      best = {QkvPlan::kSingle, bn, 1};
       best_cost = cost;
     }
   }
@@ -750,9 +1078,10 @@ int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream) 
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc != B200_OK) return rc;
-  switch (qkv_pick_bn(a.num_tokens, a.hidden, dev.num_sms)) {
-    case 0:
-      return launch_pair(a, stream, dev);
+  const QkvPlan plan = qkv_plan(a.num_tokens, a.hidden, dev);
+  if (plan.kind == QkvPlan::kPair) return launch_pair(a, stream, dev);
+  if (plan.kind == QkvPlan::kSplit) return launch_split(a, stream, plan.splits);
+  switch (plan.bn) {
     case 256:
       return launch_bn<256>(a, stream, dev);
     case 128:

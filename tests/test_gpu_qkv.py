@@ -72,14 +72,17 @@ def _check_pool(c, y, status_bits=0):
 @pytest.mark.parametrize("T,C,H,S,L,layer", [
     (1, 256, 8, 16, 2, 1),       # one decode token, cfg2-sized model (H=8, D=32)
     (5, 256, 8, 16, 1, 0),
-    (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (64-wide output tiles)
+    (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (split-K clusters)
+    (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
+    (100, 1024, 8, 16, 1, 0),    # split-K over 16 k-steps
     (129, 4096, 32, 16, 2, 1),   # two token tiles, the second ragged (128-wide tiles)
     (300, 512, 4, 16, 1, 0),
     (1000, 4096, 32, 16, 1, 0),  # prefill chunk (CTA pairs, 256 x 256 tiles)
     (600, 2048, 16, 16, 2, 1),   # CTA pairs; the second CTA of the last pair has no rows
     (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step
     (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
-    (200, 3136, 49, 16, 1, 0),   # 128-wide tiles, 3C = 73.5 tiles: ragged last output tile
+    (200, 3136, 49, 16, 1, 0),   # 3C = 36.75 x 256: ragged last output tile
+    (200, 4160, 65, 16, 1, 0),   # 128-wide tiles, 3C = 97.5 x 128: ragged last output tile
     (1000, 4160, 65, 16, 1, 0),  # CTA pairs, 3C = 48.75 tiles: ragged last output tile
 ])
 def test_qkv_kv_write_matches_fp32_projection(T, C, H, S, L, layer):
