@@ -23,8 +23,9 @@ bool prefill_tc_supported(const b200_prefill_args_t& a);
 struct QkvPlan {
   enum Kind { kSingle = 0, kPair = 1, kSplit = 2 };
   int kind;
-  int bn;
-  int splits;
+  int bn;      // output features per tile
+  int splits;  // reduction split (cluster size) of kSplit
+  int xrows;   // x box rows of kSplit
 };
 int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream);
 int launch_bounded_wait_selftest(int32_t* status, int64_t limit_ns, cudaStream_t stream);

@@ -15,8 +15,14 @@
 // output row, so the epilogue stores each 32-column run of a row straight
 // into the row's slot and k and v never exist as a separate tensor.
 //
-// Persistent CTAs (one per SM) walk the output tiles (128 tokens x BN
-// features) in the grouped order of tile_coords.  Warp roles (6 warps):
+// Three kernels share the warp roles below; qkv_plan picks one per call:
+//   CTA pairs   long token runs: 256 x 256 tiles, tcgen05.mma.cta_group::2;
+//   single CTA  128 x BN tiles (BN = 64 or 128) where those waves are
+//               cheaper than pair waves;
+//   split-K     decode-size token counts (<= 256): one output tile per
+//               cluster, the reduction split over the cluster's CTAs.
+// The persistent ones (one CTA per SM) walk the output tiles in the grouped
+// order of tile_coords.  Warp roles (6 warps):
 //   warp 0     TMA producer: the x tile (128 x 64) and the W tile (BN x 64)
 //              of each k-step, 128-byte swizzle, into a STAGES-deep ring;
 //   warp 1     TMEM allocation and MMA issue: D[acc] += A B^T with M = 128,
@@ -53,7 +59,7 @@ struct QkvCfg {
   static constexpr int A_BYTES = kBM * 128;  // x tile: 128 rows of 64 bf16
   static constexpr int B_BYTES = BN * 128;   // W tile: BN rows of 64 bf16
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = kRingBytes / STAGE;  // 4 / 6 / 8 for BN 256 / 128 / 64
+  static constexpr int STAGES = kRingBytes / STAGE;  // 6 / 8 for BN 128 / 64
   static constexpr int BAR = STAGES * STAGE;
   static constexpr int BYTES = BAR + 256;
   static constexpr int TMEM_COLS = 2 * BN;  // two f32 accumulators
@@ -603,18 +609,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ split K
-// Few tokens (decode): reading the 3C x C weight dominates, and one
-// 256-wide tile per CTA would keep only 3C / 256 SMs streaming it (48 at
-// C = 4096).  The reduction is split instead: a cluster of `splits` CTAs
-// computes one output tile, CTA r accumulating k-steps [r * kpb, +kpb) in
-// its own TMEM.  Each CTA stages its partial rows (live tokens only) in its
+// Few tokens (decode): reading the 3C x C weight dominates, and TMA brings
+// at most ~90 GB/s into one SM, so the weight stream must be spread over
+// nearly every SM with as few bytes per SM as possible.  One tile per CTA
+// of 256 features would use only 3C / 256 SMs (48 at C = 4096); instead
+// the tile width (a multiple of 32, <= 256) and a split of the reduction
+// over a cluster of `splits` CTAs are chosen per call: CTA r of a cluster
+// accumulates k-steps [r * kpb, +kpb) of one output tile in its own TMEM.
+// The x box is only as tall as the live tokens (rows of the A operand past
+// it hold stale data, which only reaches accumulator rows that are never
+// stored).  Each CTA stages its partial rows (live tokens only) in its
 // shared memory; CTA r then sums tokens r, r + splits, ... over the
 // cluster's staging areas in rank order (the same order every run), rounds
 // once to bf16 and stores them, 64 threads per token row.
-constexpr int kSplitBN = 256;
-constexpr int kStageRowWords = kSplitBN + 4;  // padded: 16-byte stores of a warp hit distinct banks
-using SplitCfg = QkvCfg<kSplitBN>;
-static_assert(kBM * kStageRowWords * 4 <= SplitCfg::BAR, "staging must fit in the operand ring");
+constexpr int kSplitMaxBN = 256;
+constexpr int kSplitMaxStages = 24;
+constexpr int kSplitBarOffset = kRingBytes;          // barriers after the ring
+constexpr int kSplitBytes = kSplitBarOffset + 512;
+constexpr int kStageRowWords = kSplitMaxBN + 4;      // padded: 16-byte stores of a warp hit distinct banks
+static_assert(kBM * kStageRowWords * 4 <= kRingBytes, "staging must fit in the operand ring");
+static_assert((2 * kSplitMaxStages + 2) * 8 + 8 <= 512, "barrier area too small");
+
+struct SplitShape {
+  int bn;           // output features per tile (multiple of 32, <= 256)
+  int xrows;        // x box rows (multiple of 8, <= 128)
+  int stage_bytes;  // (xrows + bn) * 128
+  int stages;
+  int splits;
+  int kpb;          // k-steps per split
+};
 
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
@@ -634,18 +657,20 @@ __device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_kv_write_split_kernel(const __grid_constant__ CUtensorMap tmx,
                               const __grid_constant__ CUtensorMap tmw, const QkvParams p,
-                              int splits, int kpb) {
-  using Cfg = SplitCfg;
-  constexpr int STAGES = Cfg::STAGES;
+                              const SplitShape sh) {
+  const int STAGES = sh.stages;
+  const int splits = sh.splits;
+  const int bn = sh.bn;
+  const int a_bytes = sh.xrows * 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
 
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR);
-  uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSplitBarOffset);
+  uint64_t* empty = full + kSplitMaxStages;
+  uint64_t* acc_full = empty + kSplitMaxStages;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
@@ -664,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kSplitBN)
+                 "r"(kSplitMaxBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -674,9 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int tile = blockIdx.x / splits;
   const int m0 = (tile % p.m_tiles) * kBM;
-  const int n0 = (tile / p.m_tiles) * kSplitBN;
-  const int k0 = static_cast<int>(rank) * kpb;
-  const int k1 = min(p.k_iters, k0 + kpb);
+  const int n0 = (tile / p.m_tiles) * bn;
+  const int k0 = static_cast<int>(rank) * sh.kpb;
+  const int k1 = min(p.k_iters, k0 + sh.kpb);
   const int live = static_cast<int>(p.T - m0 < kBM ? p.T - m0 : kBM);
   float* stage_rows = reinterpret_cast<float*>(smem);  // [kBM][kStageRowWords], after the MMAs
 
@@ -684,18 +709,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmx);
       tma_prefetch_desc(&tmw);
+      // Every CTA of a split reads the same x columns; starting each tile's
+      // walk at its own k-step spreads those reads over the L2 slices
+      // instead of all CTAs requesting one chunk at a time.
+      const int nk = k1 - k0;
+      const int rot = nk > 0 ? tile % nk : 0;
       int issued = 0;
-      for (int kb = k0; kb < k1; ++kb, ++issued) {
+      for (; issued < nk; ++issued) {
+        const int kb = k0 + (issued + rot) % nk;
         const int st = issued % STAGES;
         if (*abort_v || !mbar_wait(&empty[st], ((issued / STAGES) & 1) ^ 1)) {
           report(p.status, B200_DEV_WAIT_TIMEOUT);
           *abort_v = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(Cfg::STAGE));
-        uint8_t* a = smem + st * Cfg::STAGE;
+        mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(sh.stage_bytes));
+        uint8_t* a = smem + st * sh.stage_bytes;
         tma_load_2d(a, &tmx, &full[st], kb * kBK, m0);
-        tma_load_2d(a + Cfg::A_BYTES, &tmw, &full[st], kb * kBK, n0);
+        tma_load_2d(a + a_bytes, &tmw, &full[st], kb * kBK, n0);
       }
       for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
         if (!mbar_wait(&full[j % STAGES], (j / STAGES) & 1)) {
@@ -704,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
   } else if (warp == 1) {
-    constexpr uint32_t idesc = idesc_bf16(kBM, kSplitBN, false);
+    const uint32_t idesc = idesc_bf16(kBM, bn, false);
     const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
     bool ok = true;
     for (int kb = k0, j = 0; kb < k1; ++kb, ++j) {
@@ -714,8 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint64_t da = da0 + static_cast<uint64_t>((st * Cfg::STAGE) >> 4);
-      const uint64_t db = da + static_cast<uint64_t>(Cfg::A_BYTES >> 4);
+      const uint64_t da = da0 + static_cast<uint64_t>((st * sh.stage_bytes) >> 4);
+      const uint64_t db = da + static_cast<uint64_t>(a_bytes >> 4);
 #pragma unroll
       for (int kk = 0; kk < kBK / 16; ++kk)
         mma_bf16(tmem, da + static_cast<uint64_t>(kk * 2), db + static_cast<uint64_t>(kk * 2), idesc,
@@ -740,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kSplitBN; c += 32) {
+      for (int c = 0; c < bn; c += 32) {
         float v[32];
         __syncwarp();
         tmem_ld32(trow + static_cast<uint32_t>(c), v);
@@ -764,22 +795,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool all_ok = true;
     for (int q = 0; q < splits; ++q)
       all_ok = all_ok && ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) == 0;
-    if (all_ok) {
-      const int e = threadIdx.x - 64;  // 0..127
-      const int c4 = (e & 63) * 4;      // this thread's 4 columns of a row
-      const int64_t n = n0 + c4;
+    const int e = threadIdx.x - 64;  // 0..127
+    const int c4 = (e & 63) * 4;      // this thread's 4 columns of a row
+    const int64_t n = n0 + c4;
+    if (all_ok && c4 < bn && n < 3 * p.C) {
       for (int lr = static_cast<int>(rank) + (e >> 6) * splits; lr < live; lr += 2 * splits) {
-        const uint32_t off = smem_u32(stage_rows + lr * kStageRowWords + c4);
+        const uint32_t off = static_cast<uint32_t>((lr * kStageRowWords + c4) * 4);
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int q = 0; q < splits; ++q) {
-          const float4 v = ld_cluster_f4(map_to_rank(stage_rows, static_cast<uint32_t>(q)) +
-                                         (off - smem_u32(stage_rows)));
+          const float4 v = ld_cluster_f4(map_to_rank(stage_rows, static_cast<uint32_t>(q)) + off);
           s.x += v.x;
           s.y += v.y;
           s.z += v.z;
           s.w += v.w;
         }
-        if (n >= 3 * p.C) continue;
         const int64_t row = m0 + lr;
         const uint2 w2 = make_uint2(pack_bf16(s.x, s.y), pack_bf16(s.z, s.w));
         if (n < p.C) {
@@ -801,7 +830,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // no CTA leaves while a peer may still read its staging area
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSplitBN)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kSplitMaxBN)
                  : "memory");
   }
 }
@@ -946,28 +976,31 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
 }
 
 // Clusters of `cluster` split-K CTAs that can be resident at once (cached).
-int split_capacity(int cluster, size_t smem, const DeviceInfo& dev) {
+int split_capacity(int cluster, const DeviceInfo& dev) {
   static int cache[64][9] = {};
+  if (cluster == 1) return dev.num_sms;
   if (dev.device < 0 || dev.device >= 64 || cluster < 2 || cluster > 8) return 0;
   int& slot = cache[dev.device][cluster];
   if (slot == 0) {
+    const size_t smem = static_cast<size_t>(kSplitBytes) + 1024;
     cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_split_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_split)"), 0;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(static_cast<unsigned>(cluster * (dev.num_sms / cluster)), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_split_kernel, &cfg);
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(static_cast<unsigned>(cluster * (dev.num_sms / cluster)), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_split_kernel, &cfg);
+    }
     if (e != cudaSuccess) {
       (void)cudaGetLastError();
       n = 0;
@@ -977,15 +1010,33 @@ int split_capacity(int cluster, size_t smem, const DeviceInfo& dev) {
   return slot > 0 ? slot : 0;
 }
 
-int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, int splits) {
-  using Cfg = SplitCfg;
+int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const QkvPlan& plan,
+                 const DeviceInfo& dev) {
   const int64_t T = a.num_tokens, C = a.hidden;
-  const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
+  const size_t smem = static_cast<size_t>(kSplitBytes) + 1024;
+  static int configured[64] = {0};
+  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+    cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_split_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_split)");
+    configured[dev.device] = 1;
+  }
+  SplitShape sh;
+  sh.bn = plan.bn;
+  sh.xrows = plan.xrows;
+  sh.stage_bytes = (sh.xrows + sh.bn) * 128;
+  // The M = 128 MMA reads 16 KB of A rows from each stage base, past the
+  // stage when the x box is short: the last stage's A window must still
+  // end inside the ring.
+  sh.stages = std::min({kSplitMaxStages, kRingBytes / sh.stage_bytes,
+                        (kRingBytes - kBM * 128) / sh.stage_bytes + 1});
+  sh.splits = plan.splits;
   CUtensorMap tx, tw;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
     const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.xrows)};
     int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
                                dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
@@ -993,7 +1044,7 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, int spl
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
     const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kSplitBN)};
+    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.bn)};
     int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                                const_cast<void*>(a.weight), dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1013,23 +1064,23 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, int spl
   prm.nslots = a.pool.num_blocks * a.pool.block_size;
   prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
   prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
-  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, kSplitBN));
+  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, sh.bn));
   prm.k_iters = static_cast<int32_t>(C / kBK);
   prm.status = a.status;
-  const int kpb = static_cast<int>(ceil_div(prm.k_iters, splits));
+  sh.kpb = static_cast<int>(ceil_div(prm.k_iters, sh.splits));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.x = static_cast<unsigned>(sh.splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(prm.m_tiles * prm.n_tiles * splits), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(prm.m_tiles * prm.n_tiles * sh.splits), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qkv_kv_write_split_kernel, tx, tw, prm, splits, kpb);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qkv_kv_write_split_kernel, tx, tw, prm, sh);
   if (e != cudaSuccess) return cuda_fail(e, "qkv_kv_write_split launch");
   return B200_OK;
 }
@@ -1039,35 +1090,43 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, int spl
 QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
-  const int cand[3] = {256, 128, 64};
   if (m_tiles <= 2) {
-    // Few tokens (decode): the weights dominate and are read once.  Split
-    // the reduction over a cluster when that puts more SMs on the weight
-    // stream than one tile per CTA does (every split keeps >= 8 k-steps).
-    const int64_t tiles = m_tiles * ceil_div(3 * C, kSplitBN);
+    // Few tokens (decode): the weights dominate and are read once, at a
+    // per-SM rate that TMA caps.  Pick the tile width and reduction split
+    // that stage the fewest bytes per CTA with every CTA resident at once
+    // (splits keep >= 8 k-steps each).
     const int64_t k_iters = C / kBK;
-    const size_t smem = static_cast<size_t>(SplitCfg::BYTES) + 1024;
-    int best = 1;
-    for (int s = 2; s <= 8; ++s)
-      if (tiles * s <= num_sms && k_iters / s >= 8 && tiles <= split_capacity(s, smem, dev))
-        best = s;
-    if (best >= 2) return {QkvPlan::kSplit, kSplitBN, best};
-    // Otherwise the widest tile that still gives every SM a tile.
-    for (int bn : cand)
-      if (m_tiles * ceil_div(3 * C, bn) >= num_sms) return {QkvPlan::kSingle, bn, 1};
-    return {QkvPlan::kSingle, 64, 1};
+    const int xrows = m_tiles == 1 ? static_cast<int>((T + 7) / 8 * 8) : kBM;
+    QkvPlan best{QkvPlan::kSplit, 0, 0, 0};
+    int64_t best_cost = -1;
+    for (int bn = kSplitMaxBN; bn >= 32; bn -= 32) {
+      const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
+      for (int s = 1; s <= 8; ++s) {
+        if (tiles * s > num_sms || (s > 1 && k_iters / s < 8)) continue;
+        if (s > 1 && tiles > split_capacity(s, dev)) continue;
+        const int64_t cost = ceil_div(k_iters, s) * (xrows + bn);
+        if (best_cost < 0 || cost < best_cost) {
+          best = {QkvPlan::kSplit, bn, s, xrows};
+          best_cost = cost;
+        }
+      }
+    }
+    if (best_cost >= 0) return best;
+    // More 32-wide tiles than SMs: one 128-wide tile per CTA, several waves.
+    return {QkvPlan::kSingle, 128, 1, kBM};
   }
   // Otherwise: fewest shared-memory-bound clocks per SM, counting the
   // partial last wave; CTA pairs (256 x 256 tiles) unless a single-CTA
   // tile width is cheaper.
-  QkvPlan best{QkvPlan::kPair, kPairBN, 1};
+  const int cand[2] = {128, 64};
+  QkvPlan best{QkvPlan::kPair, kPairBN, 1, kBM};
   int64_t best_cost = ceil_div(ceil_div(T, 2 * kBM) * ceil_div(3 * C, kPairBN), num_sms / 2) *
                       kPairStepClocks;
   for (int bn : cand) {
     const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
     const int64_t cost = ceil_div(tiles, num_sms) * step_clocks(bn);
     if (cost < best_cost) {
-      best = {QkvPlan::kSingle, bn, 1};
+      best = {QkvPlan::kSingle, bn, 1, kBM};
       best_cost = cost;
     }
   }
@@ -1080,10 +1139,8 @@ int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream) 
   if (rc != B200_OK) return rc;
   const QkvPlan plan = qkv_plan(a.num_tokens, a.hidden, dev);
   if (plan.kind == QkvPlan::kPair) return launch_pair(a, stream, dev);
-  if (plan.kind == QkvPlan::kSplit) return launch_split(a, stream, plan.splits);
+  if (plan.kind == QkvPlan::kSplit) return launch_split(a, stream, plan, dev);
   switch (plan.bn) {
-    case 256:
-      return launch_bn<256>(a, stream, dev);
     case 128:
       return launch_bn<128>(a, stream, dev);
     default:
