@@ -619,8 +619,15 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ------------------------------------------------------------------ GPU leg
+TRAFFIC_FILES = {"cfg4": "paged_decode_cfg4_traffic.json", "cfg3": "paged_decode_cfg3_traffic.json",
+                 "qkv-prefill": "qkv_kv_write_prefill_traffic.json",
+                 "qkv-decode": "qkv_kv_write_decode_traffic.json"}
+
+
 def traffic_from_profile(workload: str) -> float | None:
-    p = REPO / "profiles" / f"paged_decode_{workload}_traffic.json"
+    if workload not in TRAFFIC_FILES:
+        return None
+    p = REPO / "profiles" / TRAFFIC_FILES[workload]
     try:
         return float(json.loads(p.read_text())["dram_bytes_per_launch_full_size"])
     except Exception:

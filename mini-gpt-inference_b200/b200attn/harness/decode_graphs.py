@@ -2,7 +2,8 @@
 
 minivllm runs the decode step eagerly, with host syncs inside it
 (model_runner.py:303, mini_runtime.py:235-238) and no CUDA Graphs
-(README.md:236-237).  Here the whole step -- embeddings, every layer's
+(the project README of mini-gpt-inference, lines 236-237).  Here the
+whole step -- embeddings, every layer's
 LayerNorm / QKV projection / fused KV write + paged decode attention /
 output projection / MLP, the final LayerNorm, LM head and the greedy
 argmax -- is captured once per batch bucket and replayed; the host reads
