@@ -623,6 +623,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // cluster's staging areas in rank order (the same order every run), rounds
 // once to bf16 and stores them, 64 threads per token row.
 constexpr int kSplitMaxBN = 256;
+// A stage holds kc (1 or 2) consecutive 64-column chunks of x and W,
+// fetched by one 3-D box per operand ({64 columns, rows, chunks}; the chunk
+// dimension strides 128 bytes through the row).  Two chunks per box halve
+// the copies per byte, whose per-box cost bounds short token counts; one
+// chunk keeps the ring at >= 3 stages when the x rows are many.
+constexpr int kSplitMaxKC = 2;
 constexpr int kSplitMaxStages = 24;
 constexpr int kSplitBarOffset = kRingBytes;          // barriers after the ring
 constexpr int kSplitBytes = kSplitBarOffset + 512;
@@ -633,7 +639,8 @@ static_assert((2 * kSplitMaxStages + 2) * 8 + 8 <= 512, "barrier area too small"
 struct SplitShape {
   int bn;           // output features per tile (multiple of 32, <= 256)
   int xrows;        // x box rows (multiple of 8, <= 128)
-  int stage_bytes;  // (xrows + bn) * 128
+  int kc;           // 64-column chunks per stage (1 or 2)
+  int stage_bytes;  // kc * (xrows + bn) * 128
   int stages;
   int splits;
   int kpb;          // k-steps per split
@@ -661,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int STAGES = sh.stages;
   const int splits = sh.splits;
   const int bn = sh.bn;
-  const int a_bytes = sh.xrows * 128;
+  const int a_bytes = sh.kc * sh.xrows * 128;  // [chunk][x row][128 B]
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5;
@@ -725,8 +732,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(sh.stage_bytes));
         uint8_t* a = smem + st * sh.stage_bytes;
-        tma_load_2d(a, &tmx, &full[st], kb * kBK, m0);
-        tma_load_2d(a + a_bytes, &tmw, &full[st], kb * kBK, n0);
+        tma_load_3d(a, &tmx, &full[st], 0, m0, kb * sh.kc);
+        tma_load_3d(a + a_bytes, &tmw, &full[st], 0, n0, kb * sh.kc);
       }
       for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
         if (!mbar_wait(&full[j % STAGES], (j / STAGES) & 1)) {
@@ -748,9 +755,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t da = da0 + static_cast<uint64_t>((st * sh.stage_bytes) >> 4);
       const uint64_t db = da + static_cast<uint64_t>(a_bytes >> 4);
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)
-        mma_bf16(tmem, da + static_cast<uint64_t>(kk * 2), db + static_cast<uint64_t>(kk * 2), idesc,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+      for (int c = 0; c < kSplitMaxKC; ++c)
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          if (c < sh.kc)
+            mma_bf16(tmem, da + static_cast<uint64_t>((c * sh.xrows * 128 + kk * 32) >> 4),
+                     db + static_cast<uint64_t>((c * bn * 128 + kk * 32) >> 4), idesc,
+                     (j > 0 || c > 0 || kk > 0) ? 1u : 0u);
+        }
       mma_commit(&empty[st]);
     }
     if (ok) {
@@ -1025,27 +1037,39 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
   SplitShape sh;
   sh.bn = plan.bn;
   sh.xrows = plan.xrows;
-  sh.stage_bytes = (sh.xrows + sh.bn) * 128;
-  // The M = 128 MMA reads 16 KB of A rows from each stage base, past the
-  // stage when the x box is short: the last stage's A window must still
-  // end inside the ring.
-  sh.stages = std::min({kSplitMaxStages, kRingBytes / sh.stage_bytes,
-                        (kRingBytes - kBM * 128) / sh.stage_bytes + 1});
+  // The M = 128 MMA reads 16 KB of A rows from each chunk's base, past the
+  // chunk when the x box is short: the last stage's last A window must
+  // still end inside the ring.
+  auto ring_stages = [&](int kc) {
+    const int sb = kc * (sh.xrows + sh.bn) * 128;
+    return std::min({kSplitMaxStages, kRingBytes / sb,
+                     (kRingBytes - kBM * 128 - (kc - 1) * sh.xrows * 128) / sb + 1});
+  };
+  sh.kc = ring_stages(2) >= 3 ? 2 : 1;
+  sh.stage_bytes = sh.kc * (sh.xrows + sh.bn) * 128;
+  sh.stages = ring_stages(sh.kc);
   sh.splits = plan.splits;
   CUtensorMap tx, tw;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.xrows)};
-    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
+    // {64 columns, token rows, 64-column chunks}: the chunk dimension
+    // steps 128 bytes along the row.
+    const uint64_t dims[3] = {static_cast<uint64_t>(kBK), static_cast<uint64_t>(T),
+                              static_cast<uint64_t>(C / kBK)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.x_row_stride * 2),
+                                 static_cast<uint64_t>(kBK * 2)};
+    const uint32_t box[3] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.xrows),
+                             static_cast<uint32_t>(sh.kc)};
+    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(a.x),
                                dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
   }
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.bn)};
-    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    const uint64_t dims[3] = {static_cast<uint64_t>(kBK), static_cast<uint64_t>(3 * C),
+                              static_cast<uint64_t>(C / kBK)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(C * 2), static_cast<uint64_t>(kBK * 2)};
+    const uint32_t box[3] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(sh.bn),
+                             static_cast<uint32_t>(sh.kc)};
+    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                                const_cast<void*>(a.weight), dims, strides, box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
@@ -1065,7 +1089,7 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
   prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
   prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
   prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, sh.bn));
-  prm.k_iters = static_cast<int32_t>(C / kBK);
+  prm.k_iters = static_cast<int32_t>(ceil_div(C, sh.kc * kBK));  // stages of kc chunks
   prm.status = a.status;
   sh.kpb = static_cast<int>(ceil_div(prm.k_iters, sh.splits));
   cudaLaunchConfig_t cfg = {};
@@ -1094,7 +1118,7 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
     // Few tokens (decode): the weights dominate and are read once, at a
     // per-SM rate that TMA caps.  Pick the tile width and reduction split
     // that stage the fewest bytes per CTA with every CTA resident at once
-    // (splits keep >= 8 k-steps each).
+    // (splits keep >= 8 chunks each).
     const int64_t k_iters = C / kBK;
     const int xrows = m_tiles == 1 ? static_cast<int>((T + 7) / 8 * 8) : kBM;
     QkvPlan best{QkvPlan::kSplit, 0, 0, 0};
