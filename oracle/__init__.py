@@ -6,7 +6,8 @@ package.
 """
 from .paged_attention import (kv_scatter, paged_decode_dense, paged_decode_online,
                               paged_decode_single, prefill_per_token, prefix_prefill,
-                              prefix_prefill_from_pool)
+                              prefix_prefill_from_pool, qkv_project_kv_write)
 
 __all__ = ["kv_scatter", "paged_decode_dense", "paged_decode_online", "paged_decode_single",
-           "prefill_per_token", "prefix_prefill", "prefix_prefill_from_pool"]
+           "prefill_per_token", "prefix_prefill", "prefix_prefill_from_pool",
+           "qkv_project_kv_write"]

@@ -249,3 +249,37 @@ def chunk_boundaries(pieces: list[int]) -> list[tuple[int, int]]:
 
 PREFILL_PIECES = [[5, 7, 19], [1, 1, 9], [16, 1, 15], [8, 8, 8, 8], [3, 5, 4, 16, 11],
                   [16, 16, 16, 16], [64, 32, 32]]
+
+
+@dataclass
+class QkvCase:
+    name: str
+    x: torch.Tensor      # [T, C] activations entering the attention's qkv Linear
+    w: torch.Tensor      # [3C, C] qkv.weight
+    pool: Pool
+    table: list
+    slots: list
+    layer_idx: int
+
+
+def qkv_case(T: int, heads: int, dim: int, block_size: int, seed: int, n_layer: int = 2,
+             layer_idx: int = 1, spare_blocks: int = 3) -> QkvCase:
+    """A first prefill chunk of T tokens through the attention's projection:
+    x ~N(0,1), qkv.weight ~N(0,1)/sqrt(C), a NaN-filled pool and the slots of
+    positions 0..T-1 over a permuted block table."""
+    g = torch.Generator().manual_seed(seed)
+    C = heads * dim
+    nb = math.ceil(T / block_size)
+    P = nb + spare_blocks
+    table = torch.randperm(P, generator=g).tolist()[:nb]
+    k = torch.full((n_layer, P, block_size, heads, dim), float("nan"))
+    v = torch.full((n_layer, P, block_size, heads, dim), float("nan"))
+    x = torch.randn((T, C), generator=g)
+    w = torch.randn((3 * C, C), generator=g) / math.sqrt(C)
+    slots = [table[i // block_size] * block_size + i % block_size for i in range(T)]
+    name = f"qkv_t{T}_h{heads}_d{dim}_s{block_size}_seed{seed}"
+    return QkvCase(name, x, w, Pool(k, v, block_size), table, slots, layer_idx)
+
+
+# (T, heads, dim, block_size, seed) of the projection fixtures.
+QKV_CASES = [(5, 2, 32, 4, 901), (37, 4, 32, 8, 902), (64, 8, 32, 16, 903)]

@@ -13,6 +13,8 @@ deterministic inputs of tests/golden/cases.py and writes
   prefill_golden.npz / prefill_golden.json  (prefill outputs, pool digests)
   e2e_golden.json                           (MiniRuntime greedy tokens and counts,
                                              configuration 2, ample and capped KV)
+  qkv_golden.json                           (pool digests after the attention's own
+                                             qkv projection + KV write)
 It also checks that cases.py reproduces the reference's input builders
 bit for bit.  The GPU box never runs this script; it only reads the files.
 """
@@ -175,6 +177,37 @@ def prefill_fixtures(ref) -> tuple[dict, dict]:
     return arrays, meta
 
 
+def qkv_fixtures(ref) -> dict:
+    """Pool contents after the reference's own projection + KV write:
+    KVCacheCausalSelfAttention.forward_prefill_chunk with its real qkv Linear
+    (weights set from the case) on a first chunk (attention.py:177-208)."""
+    from minivllm.attention import KVCacheCausalSelfAttention
+    from minivllm.kv_block_pool import KVBlockPool
+    from minivllm.kv_runtime import PrefillChunkContext
+    from minivllm.sequence import SequenceState
+
+    meta = {}
+    for T, H, D, S, seed in cases.QKV_CASES:
+        c = cases.qkv_case(T, H, D, S, seed)
+        C = H * D
+        attn = KVCacheCausalSelfAttention(C, H, block_size=4096).eval()
+        with torch.no_grad():
+            attn.qkv.weight.copy_(c.w)
+        attn.project = torch.nn.Identity()
+        pool = KVBlockPool(c.pool.k.shape[0], c.pool.k.shape[1], S, H, D)
+        pool.k, pool.v = c.pool.k.clone(), c.pool.v.clone()
+        seq = SequenceState(seq_id="s", max_tokens=10**6, prompt_tokens=[0])
+        seq.block_table = list(c.table)
+        ctx = PrefillChunkContext(seq_state=seq, kv_pool=pool, layer_idx=c.layer_idx, start_pos=0,
+                                  num_tokens=T, slot_mapping=c.slots)
+        with torch.inference_mode():
+            attn.forward_prefill_chunk(c.x[None], ctx)
+        meta[c.name] = {"T": T, "H": H, "D": D, "S": S, "seed": seed,
+                        "input_digest": cases.digest(c.x, c.w, c.pool.k, c.pool.v),
+                        "pool_after_digest": cases.digest(pool.k, pool.v)}
+    return meta
+
+
 CFG2 = {"n_embd": 256, "n_head": 8, "n_layer": 4, "vocab": 256, "pos": 296,
         "prompts": [128, 256, 128, 256], "output_len": 8, "block_size": 16,
         "token_budget": 64, "max_running": 4,
@@ -263,12 +296,19 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", choices=("all", "qkv"), default="all",
+                    help="regenerate every fixture, or only qkv_golden.json")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import minivllm  # noqa: F401  (fail early when the path is wrong)
 
     torch.set_num_threads(1)
     out = Path(args.out)
+    qkv = qkv_fixtures(args.reference)
+    (out / "qkv_golden.json").write_text(json.dumps(qkv, indent=1, sort_keys=True))
+    if args.only == "qkv":
+        print("wrote", out / "qkv_golden.json")
+        return
     arrays, meta = decode_fixtures(args.reference)
     np.savez_compressed(out / "decode_golden.npz", **arrays)
     (out / "decode_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True))

@@ -171,3 +171,31 @@ def test_torch_op_qkv_kv_write():
     y = _ref(c)
     _assert_rounded(q.reshape(20, 256), y[:, :256], "q")
     _check_pool(c, y)
+
+
+@pytest.mark.parametrize("shape", [c for c in __import__("cases").QKV_CASES])
+def test_qkv_kv_write_matches_pinned_oracle(shape):
+    """The golden projection cases (whose oracle result is pinned bit for bit
+    to the reference's own qkv Linear + write loop): the kernel on the
+    bf16-rounded operands against the oracle on the same operands."""
+    import cases
+    import oracle
+    from b200attn import qkv_kv_write_b200
+
+    T, H, D, S, seed = shape
+    c = cases.qkv_case(T, H, D, S, seed)
+    x, w = c.x.to(torch.bfloat16), c.w.to(torch.bfloat16)
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    want_q = oracle.qkv_project_kv_write(x, w, kp, vp, c.slots, c.layer_idx)
+    d = _dev()
+    pool = SimpleNamespace(k=c.pool.k.to(torch.bfloat16).to(d), v=c.pool.v.to(torch.bfloat16).to(d),
+                           block_size=S)
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(x.to(d), w.to(d), pool, c.slots, c.layer_idx)
+    torch.cuda.synchronize()
+    _assert_rounded(q.reshape(T, H * D), want_q.reshape(T, H * D), "q")
+    for got, want, what in ((pool.k, kp, "k"), (pool.v, vp, "v")):
+        got = got.float().cpu()
+        written = ~torch.isnan(want)
+        assert torch.equal(written, ~torch.isnan(got)), f"{what}: written rows differ"
+        _assert_rounded(got[written], want[written], what)

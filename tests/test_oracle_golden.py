@@ -117,3 +117,33 @@ def test_planted_mistake_is_caught():
                                 c.layer_idx)
     want = torch.from_numpy(PRE[f"{name}/sdpa"])
     assert not torch.allclose(got, want, atol=2e-5, rtol=2e-4)
+
+
+QKV_META = json.loads((GOLDEN / "qkv_golden.json").read_text())
+
+
+@pytest.mark.parametrize("name", sorted(QKV_META))
+def test_qkv_oracle_matches_reference_projection_and_write(name):
+    """The oracle's projection + KV write leaves the pool bit-identical to the
+    reference's own KVCacheCausalSelfAttention (real qkv Linear, chunk(3),
+    per-token write_layer loop; attention.py:177-208)."""
+    m = QKV_META[name]
+    c = cases.qkv_case(m["T"], m["H"], m["D"], m["S"], m["seed"])
+    assert c.name == name
+    assert cases.digest(c.x, c.w, c.pool.k, c.pool.v) == m["input_digest"]
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    q = oracle.qkv_project_kv_write(c.x, c.w, kp, vp, c.slots, c.layer_idx)
+    assert cases.digest(kp, vp) == m["pool_after_digest"]
+    assert q.shape == (m["T"], m["H"], m["D"])
+
+
+def test_qkv_planted_mistake_is_caught():
+    """Swapping the k and v thirds (a plausible split bug) changes the pool digest."""
+    name = sorted(QKV_META)[0]
+    m = QKV_META[name]
+    c = cases.qkv_case(m["T"], m["H"], m["D"], m["S"], m["seed"])
+    C = m["H"] * m["D"]
+    w_swapped = torch.cat([c.w[:C], c.w[2 * C:], c.w[C:2 * C]])
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    oracle.qkv_project_kv_write(c.x, w_swapped, kp, vp, c.slots, c.layer_idx)
+    assert cases.digest(kp, vp) != m["pool_after_digest"]
