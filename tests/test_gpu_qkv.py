@@ -193,7 +193,7 @@ def test_qkv_kv_write_matches_pinned_oracle(shape):
     with torch.inference_mode():
         q = qkv_kv_write_b200(x.to(d), w.to(d), pool, c.slots, c.layer_idx)
     torch.cuda.synchronize()
-    _assert_rounded(q.reshape(T, H * D), want_q.reshape(T, H * D), "q")
+    _assert_rounded(q.reshape(T, H * D).cpu(), want_q.reshape(T, H * D), "q")
     for got, want, what in ((pool.k, kp, "k"), (pool.v, vp, "v")):
         got = got.float().cpu()
         written = ~torch.isnan(want)
