@@ -41,9 +41,17 @@ class B200FusedQKVBackend(B200Backend):
     """B200Backend with the QKV projection and the KV write fused into one
     tcgen05 GEMM (b200_qkv_kv_write): the k and v thirds of the projection
     go from the GEMM epilogue straight into the pool, and attention then
-    reads them from there.  Needs bf16 weights and a bf16 KV pool."""
+    reads them from there.  Needs bf16 weights and a bf16 KV pool.
+
+    decode=False (the default) keeps decode steps on the B200Backend path
+    (torch projection, KV write fused into the attention kernel), which is
+    the faster one at decode batch sizes above a few tokens; prefill chunks
+    always take the fused projection."""
 
     fused_qkv = True
+
+    def __init__(self, decode: bool = False):
+        self.fused_qkv_decode = decode
 
     def decode_fused(self, x: Tensor, weight: Tensor, pool: KVBlockPool,
                      metadata: DecodeBatchMetadata, layer_idx: int) -> Tensor:
@@ -81,7 +89,7 @@ class Attention(nn.Module):
                              layer_idx: int, backend) -> Tensor:
         B, T, C = x.shape
         assert T == 1
-        if getattr(backend, "fused_qkv", False):
+        if getattr(backend, "fused_qkv_decode", False):
             out = backend.decode_fused(x.reshape(B, C), self.qkv.weight, pool, metadata, layer_idx)
         else:
             q, k, v = self._split(x, B)

@@ -52,7 +52,7 @@ def test_fused_qkv_backend_model_outputs_match_unfused():
     table = torch.randperm(12, generator=g)[:7].to(d)  # 96 + 1 tokens -> 7 blocks
     slots = (table[torch.arange(97, device=d) // S] * S + torch.arange(97, device=d) % S)
     outs = []
-    for backend in (B200Backend(), B200FusedQKVBackend()):
+    for backend in (B200Backend(), B200FusedQKVBackend(decode=True)):
         model.backend = backend
         pool = SimpleNamespace(
             k=torch.full((L, 12, S, n_head, n_embd // n_head), float("nan"), dtype=torch.bfloat16,
@@ -80,17 +80,20 @@ def test_fused_qkv_backend_model_outputs_match_unfused():
         assert ((p0 - p1).abs()[written] <= p0.abs()[written] * 0.03 + 0.02).all()
 
 
+@pytest.mark.parametrize("fused_decode", [False, True])
 @pytest.mark.parametrize("mode", ["eager", "graphs"])
-def test_cfg2_bf16_fused_qkv_runtime(mode):
+def test_cfg2_bf16_fused_qkv_runtime(mode, fused_decode):
     """Configuration 2's requests on a bf16 model through the runtime with the
     fused-QKV backend (capped KV: recompute preemption replays prefills
-    through the fused GEMM).  Lifecycle counts equal the reference's; the
-    greedy tokens equal those of the same bf16 model on the unfused backend."""
+    through the fused GEMM; with fused_decode the decode steps too).
+    Lifecycle counts equal the reference's; the greedy tokens equal those of
+    the same bf16 model on the unfused backend."""
     from b200attn.harness.model import B200Backend, B200FusedQKVBackend
 
     t_ref, c_ref, _ = run_cfg2("capped", "cuda", backend=B200Backend(), mode=mode,
                                dtype=torch.bfloat16)
-    t_fused, c_fused, rt = run_cfg2("capped", "cuda", backend=B200FusedQKVBackend(), mode=mode,
+    t_fused, c_fused, rt = run_cfg2("capped", "cuda",
+                                    backend=B200FusedQKVBackend(decode=fused_decode), mode=mode,
                                     dtype=torch.bfloat16)
     assert c_fused == GOLDEN["capped/sdpa_v2"]["counts"] == c_ref
     same = sum(a == b for r in t_ref for a, b in zip(t_ref[r], t_fused[r]))

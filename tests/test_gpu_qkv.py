@@ -199,3 +199,34 @@ def test_qkv_kv_write_matches_pinned_oracle(shape):
         written = ~torch.isnan(want)
         assert torch.equal(written, ~torch.isnan(got)), f"{what}: written rows differ"
         _assert_rounded(got[written], want[written], what)
+
+
+def test_qkv_kv_write_full_size_against_cublas():
+    """The bench's prefill shape (8192 tokens, hidden 4096, CTA pairs): every
+    q element within one bf16 ulp of cuBLAS's bf16 GEMM, and a sample of 512
+    tokens' pool rows likewise."""
+    from b200attn import qkv_kv_write_b200
+
+    T, C, H, S = 8192, 4096, 32, 16
+    d = _dev()
+    g = torch.Generator(device=d).manual_seed(77)
+    x = torch.randn((T, C), generator=g, device=d).to(torch.bfloat16)
+    w = (torch.randn((3 * C, C), generator=g, device=d) / C ** 0.5).to(torch.bfloat16)
+    P = T // S + 8
+    slots = torch.randperm(P * S, generator=g, device=d)[:T]
+    pool = SimpleNamespace(k=torch.zeros((1, P, S, H, C // H), dtype=torch.bfloat16, device=d),
+                           v=torch.zeros((1, P, S, H, C // H), dtype=torch.bfloat16, device=d),
+                           block_size=S)
+    with torch.inference_mode():
+        q = qkv_kv_write_b200(x, w, pool, slots, 0)
+        y = x @ w.t()
+    torch.cuda.synchronize()
+    ulp = 2.0 * BF16_U
+    diff = (q.reshape(T, C).float() - y[:, :C].float()).abs()
+    assert (diff <= y[:, :C].float().abs() * ulp + 1e-3).all()
+    sample = torch.randperm(T, device=d)[:512]
+    kf = pool.k.view(P * S, C)[slots[sample]].float()
+    vf = pool.v.view(P * S, C)[slots[sample]].float()
+    yk, yv = y[sample, C:2 * C].float(), y[sample, 2 * C:].float()
+    assert ((kf - yk).abs() <= yk.abs() * ulp + 1e-3).all()
+    assert ((vf - yv).abs() <= yv.abs() * ulp + 1e-3).all()
