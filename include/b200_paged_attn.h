@@ -1,7 +1,7 @@
 /*
  * b200_paged_attn.h -- C ABI of the sm_100a paged-attention backend.
  *
- * Three device operations over the minivllm KV layout
+ * Device operations over the minivllm KV layout
  *   k_pool / v_pool : contiguous [L, P, S, H, D]
  *   element (l, p, s, h, d) at (((l*P + p)*S + s)*H + h)*D + d
  * (minivllm/kv_block_pool.py:50-68 of zyyh-ops/mini-gpt-inference).
@@ -262,6 +262,13 @@ typedef struct {
 } b200_qkv_kv_write_args_t;
 
 B200_API int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* stream);
+
+/* The kernel b200_qkv_kv_write launches for num_tokens x hidden on the
+ * current device: *kind = 0 single CTAs (128 x *tile_n tiles), 1 CTA pairs
+ * (256 x 256 tiles), 2 split-K clusters of *splits CTAs (128 x *tile_n
+ * tiles).  A diagnostic with no counterpart in the reference. */
+B200_API int b200_qkv_kv_write_plan(int64_t num_tokens, int64_t hidden, int32_t* kind,
+                                    int32_t* tile_n, int32_t* splits);
 
 /* Workspace bytes the decode launch needs for these sizes. */
 B200_API size_t b200_paged_decode_workspace_size(int64_t batch, int64_t num_heads,

@@ -91,6 +91,9 @@ SIGNATURES = {
     "b200_chunked_prefill_batch": (ctypes.c_int, [ctypes.POINTER(PrefillBatchArgs), _p]),
     "b200_paged_decode_no_alloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), _p]),
     "b200_qkv_kv_write": (ctypes.c_int, [ctypes.POINTER(QkvKvWriteArgs), _p]),
+    "b200_qkv_kv_write_plan": (ctypes.c_int, [_i64, _i64, ctypes.POINTER(ctypes.c_int32),
+                                              ctypes.POINTER(ctypes.c_int32),
+                                              ctypes.POINTER(ctypes.c_int32)]),
     "b200_paged_decode_workspace_size": (
         ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int32]),
     "b200_chunked_prefill_workspace_size": (

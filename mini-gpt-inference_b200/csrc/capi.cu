@@ -209,6 +209,23 @@ int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* stream) {
   return launch_qkv_kv_write(a, static_cast<cudaStream_t>(stream));
 }
 
+int b200_qkv_kv_write_plan(int64_t num_tokens, int64_t hidden, int32_t* kind, int32_t* tile_n,
+                           int32_t* splits) {
+  clear_error();
+  B200_CHECK(kind != nullptr && tile_n != nullptr && splits != nullptr, B200_ERR_INVALID_ARGUMENT,
+             "null output pointer");
+  B200_CHECK(num_tokens >= 1 && hidden >= 64 && hidden % 64 == 0, B200_ERR_INVALID_ARGUMENT,
+             "qkv projection plan: num_tokens >= 1 and hidden a positive multiple of 64");
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != B200_OK) return rc;
+  const QkvPlan plan = qkv_plan(num_tokens, hidden, dev);
+  *kind = plan.kind;
+  *tile_n = plan.bn;
+  *splits = plan.splits;
+  return B200_OK;
+}
+
 int b200_paged_decode(const b200_decode_args_t* args, void* stream) {
   clear_error();
   if (args == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null arguments");

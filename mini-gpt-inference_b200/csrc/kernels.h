@@ -28,6 +28,8 @@ struct QkvPlan {
   int xrows;   // x box rows of kSplit
 };
 int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream);
+struct DeviceInfo;
+QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev);
 int launch_bounded_wait_selftest(int32_t* status, int64_t limit_ns, cudaStream_t stream);
 
 // Split-K planning shared by the launcher and the workspace query.

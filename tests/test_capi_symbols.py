@@ -84,6 +84,10 @@ def test_qkv_kv_write_rejects_bad_arguments_without_gpu():
         rc = lib.b200_qkv_kv_write(args(**kw), None)
         assert rc in (_lib.ERR_INVALID_ARGUMENT, _lib.ERR_UNSUPPORTED), why
     assert lib.b200_qkv_kv_write(None, None) == _lib.ERR_INVALID_ARGUMENT
+    k = ctypes.c_int32()
+    assert lib.b200_qkv_kv_write_plan(5, 96, ctypes.byref(k), ctypes.byref(k),
+                                      ctypes.byref(k)) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.b200_qkv_kv_write_plan(5, 256, None, None, None) == _lib.ERR_INVALID_ARGUMENT
     # Zero tokens is a no-op that succeeds without touching the device.
     assert lib.b200_qkv_kv_write(args(num_tokens=0), None) == _lib.OK
 

@@ -230,3 +230,24 @@ def test_qkv_kv_write_full_size_against_cublas():
     yk, yv = y[sample, C:2 * C].float(), y[sample, 2 * C:].float()
     assert ((kf - yk).abs() <= yk.abs() * ulp + 1e-3).all()
     assert ((vf - yv).abs() <= yv.abs() * ulp + 1e-3).all()
+
+
+@pytest.mark.parametrize("T,C,kind", [
+    (1, 4096, 2), (64, 4096, 2), (129, 4096, 2), (200, 6400, 0), (300, 512, 0),
+    (512, 4096, 1), (1000, 4096, 1), (8192, 4096, 1),
+])
+def test_qkv_plan_covers_each_kernel(T, C, kind):
+    """The shapes of the parity tests reach the kernel their comments name:
+    0 single CTAs, 1 CTA pairs, 2 split-K clusters."""
+    import ctypes
+
+    from b200attn import _lib
+
+    lib = _lib.load()
+    k, n, s = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    assert lib.b200_qkv_kv_write_plan(T, C, ctypes.byref(k), ctypes.byref(n), ctypes.byref(s)) == 0
+    assert k.value == kind, (k.value, n.value, s.value)
+    if kind == 2:
+        assert 1 <= s.value <= 8 and n.value % 32 == 0
+    if kind == 1:
+        assert n.value == 256
