@@ -646,12 +646,14 @@ struct SplitShape {
   int kpb;          // k-steps per split
 };
 
+// Load from a cluster peer's shared memory.  Not volatile: the staged data
+// does not change between the cluster barriers around its use, so the
+// compiler may batch these loads.
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(addr));
   return v;
 }
 
@@ -803,26 +805,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   cluster_sync_all();  // every partial of the cluster is staged
-  if (warp >= 2) {
+  {
     bool all_ok = true;
     for (int q = 0; q < splits; ++q)
       all_ok = all_ok && ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) == 0;
-    const int e = threadIdx.x - 64;  // 0..127
-    const int c4 = (e & 63) * 4;      // this thread's 4 columns of a row
-    const int64_t n = n0 + c4;
-    if (all_ok && c4 < bn && n < 3 * p.C) {
-      for (int lr = static_cast<int>(rank) + (e >> 6) * splits; lr < live; lr += 2 * splits) {
-        const uint32_t off = static_cast<uint32_t>((lr * kStageRowWords + c4) * 4);
-        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < splits; ++q) {
-          const float4 v = ld_cluster_f4(map_to_rank(stage_rows, static_cast<uint32_t>(q)) + off);
-          s.x += v.x;
-          s.y += v.y;
-          s.z += v.z;
-          s.w += v.w;
+    // This CTA's items: (token lr = rank + j * splits, 4-column group) over
+    // the tile's bn columns, flattened over all the CTA's threads.  Each
+    // thread keeps kReduceBatch items' partial loads in flight at once (the
+    // loads are independent; the staging areas do not change between the
+    // two cluster barriers).
+    const int e = threadIdx.x;
+    const int ncol4 = bn / 4;
+    const int mine = live > static_cast<int>(rank)
+                         ? (live - static_cast<int>(rank) + splits - 1) / splits : 0;
+    const int items = all_ok ? mine * ncol4 : 0;
+    constexpr int kReduceBatch = 8;
+    for (int base = e; base < items; base += kThreads * kReduceBatch) {
+      float4 acc[kReduceBatch];
+      uint32_t off[kReduceBatch];
+#pragma unroll
+      for (int u = 0; u < kReduceBatch; ++u) {
+        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int it = min(base + u * kThreads, items - 1);
+        const int lr = static_cast<int>(rank) + (it / ncol4) * splits;
+        off[u] = static_cast<uint32_t>((lr * kStageRowWords + (it % ncol4) * 4) * 4);
+      }
+      for (int q = 0; q < splits; ++q) {
+        const uint32_t peer = map_to_rank(stage_rows, static_cast<uint32_t>(q));
+        float4 v[kReduceBatch];
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) v[u] = ld_cluster_f4(peer + off[u]);
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) {
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
         }
+      }
+#pragma unroll
+      for (int u = 0; u < kReduceBatch; ++u) {
+        const int it = base + u * kThreads;
+        if (it >= items) continue;
+        const int lr = static_cast<int>(rank) + (it / ncol4) * splits;
+        const int64_t n = n0 + (it % ncol4) * 4;
+        if (n >= 3 * p.C) continue;
         const int64_t row = m0 + lr;
-        const uint2 w2 = make_uint2(pack_bf16(s.x, s.y), pack_bf16(s.z, s.w));
+        const uint2 w2 = make_uint2(pack_bf16(acc[u].x, acc[u].y), pack_bf16(acc[u].z, acc[u].w));
         if (n < p.C) {
           *reinterpret_cast<uint2*>(p.q_out + row * p.q_rs + n) = w2;
         } else {
