@@ -462,6 +462,13 @@ class ClockSampler:
         t0 = self._t0 if self._t0 is not None else float("-inf")
         t1 = self._t1 if self._t1 is not None else float("inf")
         window = [s[1:] for s in self.samples if t0 <= s[0] <= t1]
+        widened = False
+        if not window:
+            # A timed region shorter than the sampling period: take the
+            # samples within two periods of it instead, and say so.
+            pad = 2 * self.period + 0.005
+            window = [s[1:] for s in self.samples if t0 - pad <= s[0] <= t1 + pad]
+            widened = True
         if not window:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         import pynvml
@@ -470,9 +477,12 @@ class ClockSampler:
                  "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
                  "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
         reasons = sorted(n for n, bit in names.items() if any(s[2] & bit for s in window))
-        return {"sm_mhz": statistics.median(s[0] for s in window),
-                "sm_max_mhz": max(s[1] for s in window), "reasons": reasons,
-                "samples": len(window), "source": "nvml"}
+        out = {"sm_mhz": statistics.median(s[0] for s in window),
+               "sm_max_mhz": max(s[1] for s in window), "reasons": reasons,
+               "samples": len(window), "source": "nvml"}
+        if widened:
+            out["window"] = "timed region shorter than the sampling period; samples within 2 periods"
+        return out
 
 
 def gpu_indices(world: int) -> list:
