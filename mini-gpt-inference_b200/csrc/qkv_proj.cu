@@ -886,6 +886,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 int step_clocks(int bn) { return (kBM + bn) / 2; }
 constexpr int kPairStepClocks = 128;
 
+// Tensor map of a bf16 [rows, cols] matrix (row stride in elements, a
+// multiple of 8): boxes of 64 columns x box_rows rows, 128-byte swizzle.
+int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride,
+                int box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(row_stride * 2)};
+  const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(box_rows)};
+  return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                           strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Kernel parameters of one call: tiles of tile_m tokens x tile_n features,
+// k-steps of step_k reduction columns.
+QkvParams make_params(const b200_qkv_kv_write_args_t& a, int tile_m, int tile_n, int step_k) {
+  QkvParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
+  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
+  prm.slots = a.slot_mapping;
+  prm.q_rs = a.q_row_stride;
+  prm.ss = a.slot_stride;
+  prm.T = a.num_tokens;
+  prm.C = a.hidden;
+  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
+  prm.nslots = a.pool.num_blocks * a.pool.block_size;
+  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
+  prm.m_tiles = static_cast<int32_t>(ceil_div(a.num_tokens, tile_m));
+  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * a.hidden, tile_n));
+  prm.k_iters = static_cast<int32_t>(ceil_div(a.hidden, step_k));
+  prm.status = a.status;
+  return prm;
+}
+
 template <int BN>
 int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const DeviceInfo& dev) {
   using Cfg = QkvCfg<BN>;
@@ -895,23 +929,9 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
 
   CUtensorMap tx, tw;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
-    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
-                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != B200_OK) return rc;
-  }
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(BN)};
-    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                               const_cast<void*>(a.weight), dims, strides, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != B200_OK) return rc;
-  }
+  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
+  if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, BN);
+  if (rc != B200_OK) return rc;
   static int configured[64] = {0};
   if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
     cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_kernel<BN>,
@@ -920,23 +940,7 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write)");
     configured[dev.device] = 1;
   }
-  QkvParams prm;
-  memset(&prm, 0, sizeof(prm));
-  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
-  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
-  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
-  prm.slots = a.slot_mapping;
-  prm.q_rs = a.q_row_stride;
-  prm.ss = a.slot_stride;
-  prm.T = T;
-  prm.C = C;
-  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
-  prm.nslots = a.pool.num_blocks * a.pool.block_size;
-  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
-  prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
-  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, BN));
-  prm.k_iters = static_cast<int32_t>(C / kBK);
-  prm.status = a.status;
+  const QkvParams prm = make_params(a, kBM, BN, kBK);
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.num_sms));
   qkv_kv_write_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);
@@ -952,23 +956,9 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
   if (smem > static_cast<size_t>(dev.max_smem_optin))
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
   CUtensorMap tx, tw;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(T)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(a.x_row_stride * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBM)};
-    int rc = encode_tensor_map(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.x),
-                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != B200_OK) return rc;
-  }
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(3 * C)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(C * 2)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kBK), 128u};
-    int rc = encode_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                               const_cast<void*>(a.weight), dims, strides, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != B200_OK) return rc;
-  }
+  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
+  if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, 128);  // this CTA's half
+  if (rc != B200_OK) return rc;
   static int max_pairs[64] = {0};
   int pairs = dev.num_sms / 2;
   if (dev.device >= 0 && dev.device < 64) {
@@ -991,23 +981,7 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
     }
     pairs = max_pairs[dev.device];
   }
-  QkvParams prm;
-  memset(&prm, 0, sizeof(prm));
-  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
-  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
-  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
-  prm.slots = a.slot_mapping;
-  prm.q_rs = a.q_row_stride;
-  prm.ss = a.slot_stride;
-  prm.T = T;
-  prm.C = C;
-  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
-  prm.nslots = a.pool.num_blocks * a.pool.block_size;
-  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
-  prm.m_tiles = static_cast<int32_t>(ceil_div(T, 2 * kBM));
-  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, kPairBN));
-  prm.k_iters = static_cast<int32_t>(C / kBK);
-  prm.status = a.status;
+  const QkvParams prm = make_params(a, 2 * kBM, kPairBN, kBK);
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, pairs));
   qkv_kv_write_pair_kernel<<<grid, kThreads, smem, stream>>>(tx, tw, prm);
@@ -1103,23 +1077,7 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != B200_OK) return rc;
   }
-  QkvParams prm;
-  memset(&prm, 0, sizeof(prm));
-  prm.q_out = static_cast<__nv_bfloat16*>(a.q_out);
-  prm.k_pool = static_cast<__nv_bfloat16*>(a.pool.k);
-  prm.v_pool = static_cast<__nv_bfloat16*>(a.pool.v);
-  prm.slots = a.slot_mapping;
-  prm.q_rs = a.q_row_stride;
-  prm.ss = a.slot_stride;
-  prm.T = T;
-  prm.C = C;
-  prm.row0 = a.layer_idx * a.pool.num_blocks * a.pool.block_size;
-  prm.nslots = a.pool.num_blocks * a.pool.block_size;
-  prm.slots_i64 = a.slot_dtype == B200_INDEX_I64;
-  prm.m_tiles = static_cast<int32_t>(ceil_div(T, kBM));
-  prm.n_tiles = static_cast<int32_t>(ceil_div(3 * C, sh.bn));
-  prm.k_iters = static_cast<int32_t>(ceil_div(C, sh.kc * kBK));  // stages of kc chunks
-  prm.status = a.status;
+  const QkvParams prm = make_params(a, kBM, sh.bn, sh.kc * kBK);  // k-steps of kc chunks
   sh.kpb = static_cast<int>(ceil_div(prm.k_iters, sh.splits));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
