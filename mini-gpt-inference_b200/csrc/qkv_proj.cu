@@ -320,8 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // with 256-wide tiles is limited by.  Both CTAs' copies complete on CTA 0's
 // stage barrier; CTA 0's MMA commits release the stage in both CTAs and
 // publish each accumulator to both epilogues; each epilogue warp of either
-// CTA returns an accumulator to CTA 0 with one remote arrival.  No copy
-// uses cluster multicast.
+// CTA returns an accumulator to CTA 0 with one remote arrival.  Each CTA
+// loads only its own rows: every TMA copy writes the issuing CTA's shared
+// memory alone.
 constexpr int kPairBN = 256;
 struct PairCfg {
   static constexpr int A_BYTES = kBM * 128;        // this CTA's 128 x rows
