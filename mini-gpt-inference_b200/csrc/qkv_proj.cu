@@ -40,6 +40,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -898,6 +900,10 @@ int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
                            strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Guards the first-call setup per device (kernel attributes, occupancy
+// queries); later calls read the cached results without locking.
+std::mutex g_setup_mu;
+
 // Kernel parameters of one call: tiles of tile_m tokens x tile_n features,
 // k-steps of step_k reduction columns.
 QkvParams make_params(const b200_qkv_kv_write_args_t& a, int tile_m, int tile_n, int step_k) {
@@ -933,13 +939,14 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
   int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
   if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, BN);
   if (rc != B200_OK) return rc;
-  static int configured[64] = {0};
-  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+  static std::atomic<int> configured[64];
+  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
     cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_kernel<BN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write)");
-    configured[dev.device] = 1;
+    configured[dev.device].store(1, std::memory_order_release);
   }
   const QkvParams prm = make_params(a, kBM, BN, kBK);
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
@@ -960,10 +967,11 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
   int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
   if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, 128);  // this CTA's half
   if (rc != B200_OK) return rc;
-  static int max_pairs[64] = {0};
+  static std::atomic<int> max_pairs[64];
   int pairs = dev.num_sms / 2;
   if (dev.device >= 0 && dev.device < 64) {
-    if (max_pairs[dev.device] == 0) {
+    if (max_pairs[dev.device].load(std::memory_order_acquire) == 0) {
+      std::lock_guard<std::mutex> lock(g_setup_mu);
       cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_pair_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
@@ -978,9 +986,9 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
         (void)cudaGetLastError();
         n = dev.num_sms / 2;
       }
-      max_pairs[dev.device] = n;
+      max_pairs[dev.device].store(n, std::memory_order_release);
     }
-    pairs = max_pairs[dev.device];
+    pairs = max_pairs[dev.device].load(std::memory_order_acquire);
   }
   const QkvParams prm = make_params(a, 2 * kBM, kPairBN, kBK);
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
@@ -993,11 +1001,12 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
 
 // Clusters of `cluster` split-K CTAs that can be resident at once (cached).
 int split_capacity(int cluster, const DeviceInfo& dev) {
-  static int cache[64][9] = {};
+  static std::atomic<int> cache[64][9];
   if (cluster == 1) return dev.num_sms;
   if (dev.device < 0 || dev.device >= 64 || cluster < 2 || cluster > 8) return 0;
-  int& slot = cache[dev.device][cluster];
-  if (slot == 0) {
+  std::atomic<int>& slot = cache[dev.device][cluster];
+  if (slot.load(std::memory_order_acquire) == 0) {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
     const size_t smem = static_cast<size_t>(kSplitBytes) + 1024;
     cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_split_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1021,22 +1030,24 @@ int split_capacity(int cluster, const DeviceInfo& dev) {
       (void)cudaGetLastError();
       n = 0;
     }
-    slot = n > 0 ? n : -1;
+    slot.store(n > 0 ? n : -1, std::memory_order_release);
   }
-  return slot > 0 ? slot : 0;
+  const int cap = slot.load(std::memory_order_acquire);
+  return cap > 0 ? cap : 0;
 }
 
 int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const QkvPlan& plan,
                  const DeviceInfo& dev) {
   const int64_t T = a.num_tokens, C = a.hidden;
   const size_t smem = static_cast<size_t>(kSplitBytes) + 1024;
-  static int configured[64] = {0};
-  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+  static std::atomic<int> configured[64];
+  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
     cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_split_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_split)");
-    configured[dev.device] = 1;
+    configured[dev.device].store(1, std::memory_order_release);
   }
   SplitShape sh;
   sh.bn = plan.bn;

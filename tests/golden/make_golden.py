@@ -13,8 +13,8 @@ deterministic inputs of tests/golden/cases.py and writes
   prefill_golden.npz / prefill_golden.json  (prefill outputs, pool digests)
   e2e_golden.json                           (MiniRuntime greedy tokens and counts,
                                              configuration 2, ample and capped KV)
-  qkv_golden.json                           (pool digests after the attention's own
-                                             qkv projection + KV write)
+  qkv_golden.json / qkv_golden.npz          (pool digests and written K/V rows after
+                                             the attention's own qkv projection + KV write)
 It also checks that cases.py reproduces the reference's input builders
 bit for bit.  The GPU box never runs this script; it only reads the files.
 """
@@ -186,7 +186,7 @@ def qkv_fixtures(ref) -> dict:
     from minivllm.kv_runtime import PrefillChunkContext
     from minivllm.sequence import SequenceState
 
-    meta = {}
+    meta, arrays = {}, {}
     for T, H, D, S, seed in cases.QKV_CASES:
         c = cases.qkv_case(T, H, D, S, seed)
         C = H * D
@@ -205,7 +205,12 @@ def qkv_fixtures(ref) -> dict:
         meta[c.name] = {"T": T, "H": H, "D": D, "S": S, "seed": seed,
                         "input_digest": cases.digest(c.x, c.w, c.pool.k, c.pool.v),
                         "pool_after_digest": cases.digest(pool.k, pool.v)}
-    return meta
+        # The written rows themselves: fp32 matmul bits differ between host
+        # CPUs, so the tests compare these values within fp32 tolerance.
+        rows = torch.tensor(c.slots)
+        arrays[f"{c.name}/k_rows"] = pool.k[c.layer_idx].reshape(-1, C)[rows].numpy()
+        arrays[f"{c.name}/v_rows"] = pool.v[c.layer_idx].reshape(-1, C)[rows].numpy()
+    return meta, arrays
 
 
 CFG2 = {"n_embd": 256, "n_head": 8, "n_layer": 4, "vocab": 256, "pos": 296,
@@ -304,8 +309,9 @@ def main():
 
     torch.set_num_threads(1)
     out = Path(args.out)
-    qkv = qkv_fixtures(args.reference)
+    qkv, qkv_arrays = qkv_fixtures(args.reference)
     (out / "qkv_golden.json").write_text(json.dumps(qkv, indent=1, sort_keys=True))
+    np.savez_compressed(out / "qkv_golden.npz", **qkv_arrays)
     if args.only == "qkv":
         print("wrote", out / "qkv_golden.json")
         return

@@ -59,11 +59,16 @@ def test_decode_oracle_matches_reference(case):
     assert torch.isfinite(online).all() and torch.isfinite(dense).all()
     want_online = torch.from_numpy(DEC[f"{case.name}/online"])
     want_dense = torch.from_numpy(DEC[f"{case.name}/dense"])
-    torch.testing.assert_close(online, want_online, atol=ATOL, rtol=RTOL)
-    torch.testing.assert_close(dense, want_dense, atol=ATOL, rtol=RTOL)
+    # The scale-8 large-logit case (outputs up to ~21) is as sensitive to the
+    # fp32 summation order as the reference's own test allows for it
+    # (tests/test_triton_paged_decode.py:66-71, atol 5e-4); torch's CPU
+    # reductions take a different order on other host CPUs.
+    atol = 5e-4 if "_sc8.0_" in case.name else ATOL
+    torch.testing.assert_close(online, want_online, atol=atol, rtol=RTOL)
+    torch.testing.assert_close(dense, want_dense, atol=atol, rtol=RTOL)
     key = f"{case.name}/reference"
     if key in DEC.files:
-        torch.testing.assert_close(online, torch.from_numpy(DEC[key]), atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(online, torch.from_numpy(DEC[key]), atol=atol, rtol=RTOL)
 
 
 def test_unit_cases_online_equals_per_request_single():
@@ -120,25 +125,41 @@ def test_planted_mistake_is_caught():
 
 
 QKV_META = json.loads((GOLDEN / "qkv_golden.json").read_text())
+QKV = np.load(GOLDEN / "qkv_golden.npz")
+
+
+def _qkv_written(c, kp, vp):
+    C = kp.shape[3] * kp.shape[4]
+    rows = torch.tensor(c.slots)
+    return (kp[c.layer_idx].reshape(-1, C)[rows], vp[c.layer_idx].reshape(-1, C)[rows])
 
 
 @pytest.mark.parametrize("name", sorted(QKV_META))
 def test_qkv_oracle_matches_reference_projection_and_write(name):
-    """The oracle's projection + KV write leaves the pool bit-identical to the
-    reference's own KVCacheCausalSelfAttention (real qkv Linear, chunk(3),
-    per-token write_layer loop; attention.py:177-208)."""
+    """The oracle's projection + KV write matches the reference's own
+    KVCacheCausalSelfAttention (real qkv Linear, chunk(3), per-token
+    write_layer loop; attention.py:177-208): the rows written at the slots
+    agree within the reference's fp32 tolerance (the fixture's digest is
+    bit-exact on the host that made it; fp32 matmul bits differ between host
+    CPUs), and every other pool row keeps its NaN."""
     m = QKV_META[name]
     c = cases.qkv_case(m["T"], m["H"], m["D"], m["S"], m["seed"])
     assert c.name == name
     assert cases.digest(c.x, c.w, c.pool.k, c.pool.v) == m["input_digest"]
     kp, vp = c.pool.k.clone(), c.pool.v.clone()
     q = oracle.qkv_project_kv_write(c.x, c.w, kp, vp, c.slots, c.layer_idx)
-    assert cases.digest(kp, vp) == m["pool_after_digest"]
+    k_rows, v_rows = _qkv_written(c, kp, vp)
+    torch.testing.assert_close(k_rows, torch.from_numpy(QKV[f"{name}/k_rows"]), atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(v_rows, torch.from_numpy(QKV[f"{name}/v_rows"]), atol=ATOL, rtol=RTOL)
+    written = torch.zeros(kp.shape[:3], dtype=torch.bool)
+    for s_ in c.slots:
+        written[c.layer_idx, s_ // m["S"], s_ % m["S"]] = True
+    assert torch.isnan(kp[~written]).all() and torch.isnan(vp[~written]).all()
     assert q.shape == (m["T"], m["H"], m["D"])
 
 
 def test_qkv_planted_mistake_is_caught():
-    """Swapping the k and v thirds (a plausible split bug) changes the pool digest."""
+    """Swapping the k and v thirds (a plausible split bug) is caught."""
     name = sorted(QKV_META)[0]
     m = QKV_META[name]
     c = cases.qkv_case(m["T"], m["H"], m["D"], m["S"], m["seed"])
@@ -146,4 +167,5 @@ def test_qkv_planted_mistake_is_caught():
     w_swapped = torch.cat([c.w[:C], c.w[2 * C:], c.w[C:2 * C]])
     kp, vp = c.pool.k.clone(), c.pool.v.clone()
     oracle.qkv_project_kv_write(c.x, w_swapped, kp, vp, c.slots, c.layer_idx)
-    assert cases.digest(kp, vp) != m["pool_after_digest"]
+    k_rows, _ = _qkv_written(c, kp, vp)
+    assert not torch.allclose(k_rows, torch.from_numpy(QKV[f"{name}/k_rows"]), atol=ATOL, rtol=RTOL)
