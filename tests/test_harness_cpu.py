@@ -137,3 +137,22 @@ def test_graph_buckets_cover_every_batch():
         sizes = bucket_sizes(rows)
         assert sizes == sorted(set(sizes)) and sizes[-1] == rows
         assert all(any(n >= b for n in sizes) for b in range(1, rows + 1))
+
+
+@pytest.mark.parametrize("fused_decode", [False, True])
+def test_fused_qkv_routing_keeps_reference_tokens(fused_decode):
+    """The model's fused-QKV branches (projection + KV write in one call, as
+    B200FusedQKVBackend does on the GPU), driven by the oracle: capped KV
+    with recompute preemption still gives the reference's greedy tokens and
+    counts, and the decode steps take the fused branch only when asked."""
+    from oracle_backend import OracleFusedQKVBackend
+
+    backend = OracleFusedQKVBackend(decode=fused_decode)
+    tokens, counts, _ = run_cfg2("capped", "cpu", backend=backend)
+    want = GOLDEN["capped/sdpa_v2"]
+    assert tokens == want["tokens"] and counts == want["counts"]
+    assert backend.calls["prefill_fused"] > 0
+    if fused_decode:
+        assert backend.calls["decode_fused"] > 0 and backend.calls["decode"] == 0
+    else:
+        assert backend.calls["decode_fused"] == 0 and backend.calls["decode"] > 0
