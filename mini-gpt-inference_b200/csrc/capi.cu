@@ -197,6 +197,9 @@ int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* stream) {
              "qkv projection: num_heads * head_dim must equal the hidden size");
   B200_CHECK(a.hidden <= (int64_t(1) << 20) && a.num_tokens < (int64_t(1) << 31) / 2,
              B200_ERR_UNSUPPORTED, "qkv projection: sizes too large");
+  // Tile indices are 32-bit: bound the finest tiling (128 tokens x 32 features).
+  B200_CHECK(ceil_div(a.num_tokens, 128) * ceil_div(3 * a.hidden, 32) < (int64_t(1) << 31),
+             B200_ERR_UNSUPPORTED, "qkv projection: too many output tiles (split the tokens)");
   B200_CHECK(a.x_row_stride >= a.hidden && a.x_row_stride % 8 == 0 &&
                  a.q_row_stride >= a.hidden && a.q_row_stride % 8 == 0,
              B200_ERR_UNSUPPORTED,

@@ -79,6 +79,10 @@ def test_qkv_kv_write_rejects_bad_arguments_without_gpu():
         "f32 pool": dict(pool=_lib.KVPool(1 << 20, 2 << 20, 2, 8, 16, 4, 64, _lib.DTYPE_F32)),
         "layer outside pool": dict(layer_idx=2),
         "bad slot dtype": dict(slot_dtype=7),
+        "too many output tiles": dict(num_tokens=(1 << 30) - 1,
+                                      pool=_lib.KVPool(1 << 20, 2 << 20, 2, 8, 16, 4096, 128,
+                                                       _lib.DTYPE_BF16),
+                                      hidden=1 << 19, x_row_stride=1 << 19, q_row_stride=1 << 19),
     }
     for why, kw in bad.items():
         rc = lib.b200_qkv_kv_write(args(**kw), None)
