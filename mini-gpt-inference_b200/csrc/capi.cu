@@ -170,6 +170,9 @@ int b200_kv_scatter(const b200_kv_scatter_args_t* args, void* stream) {
   if (rc != B200_OK) return rc;
   if (a.num_tokens < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
   if (a.num_tokens == 0) return B200_OK;
+  // One CTA per token: the grid's x extent bounds N (a pool holds < 2^31 rows anyway).
+  if (a.num_tokens >= (int64_t(1) << 31) - 1)
+    return fail(B200_ERR_UNSUPPORTED, "kv scatter: num_tokens must be < 2^31 - 1");
   if (a.k == nullptr || a.v == nullptr || a.slot_mapping == nullptr)
     return fail(B200_ERR_INVALID_ARGUMENT, "k, v and slot_mapping must be non-null");
   if (!valid_dtype(a.kv_in_dtype))

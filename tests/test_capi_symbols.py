@@ -109,6 +109,10 @@ def test_last_error_and_invalid_arguments_without_gpu():
     assert "KV pool" in _lib.last_error(lib)
     sargs = _lib.ScatterArgs()
     assert lib.b200_kv_scatter(ctypes.byref(sargs), None) == _lib.ERR_INVALID_ARGUMENT
+    sargs.pool = _lib.KVPool(1 << 20, 2 << 20, 1, 4, 16, 2, 64, _lib.DTYPE_BF16)
+    sargs.num_tokens = 1 << 31
+    assert lib.b200_kv_scatter(ctypes.byref(sargs), None) == _lib.ERR_UNSUPPORTED
+    assert "2^31" in _lib.last_error(lib)
 
 
 def test_workspace_size_queries():
