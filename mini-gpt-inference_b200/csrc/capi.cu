@@ -88,6 +88,10 @@ int check_prefill(const b200_prefill_args_t& a) {
   if (rc != B200_OK) return rc;
   B200_CHECK(a.num_tokens >= 1, B200_ERR_INVALID_ARGUMENT, "prefill chunk must be nonempty");
   B200_CHECK(a.prefix_len >= 0, B200_ERR_INVALID_ARGUMENT, "prefix_len must be >= 0");
+  // Positions are 32-bit in the kernels; the fp32 path runs the chunk as a
+  // decode batch, whose size limit it shares.
+  B200_CHECK(a.num_tokens < (int64_t(1) << 24) && a.prefix_len + a.num_tokens < (int64_t(1) << 31),
+             B200_ERR_UNSUPPORTED, "prefill chunk too large (num_tokens < 2^24, positions < 2^31)");
   B200_CHECK(a.q != nullptr && a.out != nullptr, B200_ERR_INVALID_ARGUMENT,
              "q and out must be non-null");
   B200_CHECK(valid_dtype(a.q_dtype) && valid_dtype(a.out_dtype), B200_ERR_INVALID_ARGUMENT,

@@ -113,6 +113,12 @@ def test_last_error_and_invalid_arguments_without_gpu():
     sargs.num_tokens = 1 << 31
     assert lib.b200_kv_scatter(ctypes.byref(sargs), None) == _lib.ERR_UNSUPPORTED
     assert "2^31" in _lib.last_error(lib)
+    pargs = _lib.PrefillArgs()
+    pargs.pool = _lib.KVPool(1 << 20, 2 << 20, 1, 4, 16, 2, 64, _lib.DTYPE_BF16)
+    pargs.num_tokens, pargs.prefix_len = 1 << 24, 0
+    assert lib.b200_chunked_prefill(ctypes.byref(pargs), None) == _lib.ERR_UNSUPPORTED
+    pargs.num_tokens, pargs.prefix_len = 16, (1 << 31) - 8
+    assert lib.b200_chunked_prefill(ctypes.byref(pargs), None) == _lib.ERR_UNSUPPORTED
 
 
 def test_workspace_size_queries():
