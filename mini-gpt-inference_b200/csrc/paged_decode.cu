@@ -35,6 +35,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -651,14 +652,21 @@ template <typename KV, int DPAD, int G, int WPH, int STAGES>
 static int launch_cfg(const DecodeParams& prm, const CUtensorMap& tk, const CUtensorMap& tv,
                       int64_t grid, size_t smem, cudaStream_t stream) {
   auto kern = paged_decode_kernel<KV, DPAD, G, WPH, STAGES>;
-  static int configured[64] = {0};
+  // The attribute only ever grows (under a lock, so that concurrent first
+  // calls with different sizes cannot lower it below a size in use).
+  static std::atomic<int> configured[64];
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && configured[dev] < static_cast<int>(smem)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(paged_decode)");
-    configured[dev] = static_cast<int>(smem);
+  if (dev >= 0 && dev < 64 &&
+      configured[dev].load(std::memory_order_acquire) < static_cast<int>(smem)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[dev].load(std::memory_order_relaxed) < static_cast<int>(smem)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(paged_decode)");
+      configured[dev].store(static_cast<int>(smem), std::memory_order_release);
+    }
   }
   kern<<<static_cast<unsigned>(grid), DecodeCfg<KV, DPAD, G, WPH, STAGES>::THREADS, smem,
          stream>>>(tk, tv, prm);

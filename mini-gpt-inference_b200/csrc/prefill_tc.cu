@@ -39,6 +39,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -830,13 +832,16 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B200_OK) return rc;
 
-  static int configured[64] = {0};
-  if (dev.device >= 0 && dev.device < 64 && !configured[dev.device]) {
+  static std::atomic<int> configured[64];
+  static std::mutex mu;
+  if (dev.device >= 0 && dev.device < 64 &&
+      !configured[dev.device].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
     cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<D_, BN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
-    configured[dev.device] = 1;
+    configured[dev.device].store(1, std::memory_order_release);
   }
 
   for (int64_t base = 0; base < n; base += kMaxSeqs) {
