@@ -624,7 +624,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // stored).  Each CTA stages its partial rows (live tokens only) in its
 // shared memory; CTA r then sums tokens r, r + splits, ... over the
 // cluster's staging areas in rank order (the same order every run), rounds
-// once to bf16 and stores them, 64 threads per token row.
+// once to bf16 and stores them; the (token, 4-column group) items are spread
+// over all of the CTA's threads, several loads in flight per thread.
 constexpr int kSplitMaxBN = 256;
 // A stage holds kc (1 or 2) consecutive 64-column chunks of x and W,
 // fetched by one 3-D box per operand ({64 columns, rows, chunks}; the chunk
