@@ -511,21 +511,35 @@ def usable_cpus() -> int:
     return max(1, n)
 
 
-def cpu_reference_sample(workload: str, steps: int, warmup: int) -> dict:
+def cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), or the platform's."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
+def cpu_reference_sample(workload: str, steps: int, warmup: int,
+                         threads: int | None = None) -> dict:
     """Times the reference algorithm (its CPU restatement under oracle/) on
     the host cores, all threads, on a bounded sample of the workload."""
     sys.path.insert(0, str(REPO))
     import oracle
     from b200attn.ops import decode_bytes
 
-    threads = usable_cpus()
+    threads = threads or usable_cpus()
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(5)
     if workload in ("cfg4", "cfg3"):
         # paged_attention_batch_online_v1 on 4 requests x 32768 tokens (cfg4)
         # or 8 ragged requests (cfg3); the reference cannot mix bf16 KV with
         # fp32 q, so the bf16 sample pool is upcast to fp32 first.
-        lens = [32768] * 4 if workload == "cfg4" else \
+        # (one request for the single-thread figure, which runs ~4x slower)
+        lens = [32768] * (1 if threads == 1 else 4) if workload == "cfg4" else \
             torch.randint(1, 4097, (8,), generator=g).tolist()
         counts = [math.ceil(n / S) for n in lens]
         P = sum(counts)
@@ -707,6 +721,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_sample(args.workload, steps=3, warmup=0)
         cpu.pop("seconds_per_step")
+        # The reference's own harnesses time one thread; record that too.
+        one = cpu_reference_sample(args.workload, steps=1, warmup=0, threads=1)
+        cpu["value_1_thread"] = one["value"]
+        cpu["cpu_model"] = cpu_model()
     if rank == 0:
         metric = metric_name(args.workload, wl.unit)
         line = {

@@ -83,3 +83,9 @@ def test_warmup_below_three_is_rejected():
                           "--workload", "scatter", "--steps", "1", "--warmup", "2"],
                          capture_output=True, text=True, timeout=120, cwd=REPO)
     assert out.returncode != 0 and "warmup" in out.stderr
+
+
+def test_cpu_baseline_sample_with_one_thread(bench):
+    r = bench.cpu_reference_sample("scatter", steps=1, warmup=0, threads=1)
+    assert r["cores"] == 1 and r["value"] > 0 and r["kind"] == "port"
+    assert isinstance(bench.cpu_model(), str) and bench.cpu_model()
