@@ -551,7 +551,8 @@ def cpu_reference_sample(workload: str, steps: int, warmup: int,
         fn = lambda: oracle.paged_decode_online(q, kf, vf, tables, ctx, 0)
         work = decode_bytes(lens, H, D, S, kv_bytes=2, q_bytes=2, out_bytes=2)
         unit = "GB/s"
-        sample = (f"{len(lens)} request(s), contexts {lens if len(lens) < 4 else 'U[1,4096]'},"
+        ctx_desc = f"{len(lens)} x {lens[0]}" if workload == "cfg4" else "U[1,4096]"
+        sample = (f"{len(lens)} request(s), contexts {ctx_desc},"
                   " H=32, D=128, S=16, bf16 KV upcast to fp32, paged_attention_batch_online_v1"
                   " restatement (oracle/)")
     elif workload.startswith("cfg5"):
