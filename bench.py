@@ -2,18 +2,19 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload cfg4|cfg3|cfg5-t512|cfg5-t64|scatter|qkv-prefill|qkv-decode]
+                    [--only]
 
 One step = one launch of the hot path over one batch of the workload, with
 inputs resident in HBM (``value``), and the same step through the public
 Python API with the step's inputs copied from pinned host memory and its
-result copied back, plus a host synchronisation (``e2e``):
+result copied back, plus a host synchronisation (``e2e``).  Workloads:
 
-* cfg4 (default): configuration 4 -- fused KV write + paged decode, bf16 KV,
-  64 requests per GPU, every context 32768 tokens, 32 heads x 128 dims, block
-  size 16, randomly permuted block tables; 34.7 GB of KV per GPU (larger than
-  the 126 MB L2, so no flush is needed between steps).  Requests are sharded
-  across GPUs (weak scaling: each rank owns 64 requests of the global batch).
-* cfg3: configuration 3 at batch 256 -- ragged contexts ~U[1, 4096].
+* cfg4 (the headline): configuration 4 -- fused KV write + paged decode, bf16
+  KV, 64 requests per GPU, every context 32768 tokens, 32 heads x 128 dims,
+  block size 16, randomly permuted block tables; 37.8 GB of KV per GPU
+  (larger than the 126 MB L2, so no flush is needed between steps).
+* cfg3 / cfg3-f32: configuration 3 at batch 256 -- ragged contexts
+  ~U[1, 4096], bf16 or fp32 KV.
 * cfg5-t512 / cfg5-t64: configuration 5 -- one batched tcgen05 chunked
   prefill launch over 16 sequences, chunk 512 or 64 tokens, prefixes
   16*U{0..252}; the KV pool is ~2-4 GB (larger than L2).
@@ -21,15 +22,25 @@ result copied back, plus a host synchronisation (``e2e``):
 * qkv-prefill / qkv-decode: the attention's QKV projection with the KV write
   in its epilogue (tcgen05 GEMM), hidden 4096, over 8192 prefill tokens
   (TFLOP/s, tensor roofline) or 64 decode tokens (GB/s, HBM roofline: the
-  100 MB weight read dominates); the line also carries the unfused sequence
-  (cuBLAS matmul, then the scatter) timed in the same run.
+  100 MB weight read dominates); the object also carries the unfused
+  sequence (cuBLAS matmul, then the scatter) timed in the same run.
 
-Under torchrun (N>1) each rank runs its shard on its own GPU; the only
-collective is the all-reduce(MAX) of the timings.  Rank 0 prints one JSON
-line.  ``--impl reference`` times the reference algorithm's CPU restatement
-(oracle/: paged_attention_batch_online_v1, the SDPA v2 prefill, the KV
-write loop of minivllm) on the host cores instead; under torchrun only
-rank 0 runs it.
+The JSON line's top level is the --workload (default cfg4; weak scaling:
+every rank owns 64 requests).  Unless --only is given, the same line also
+carries
+* ``workloads``: every other workload above, one sub-object each with its
+  own ms_per_step, roofline, e2e and clocks;
+* ``strong_scaling`` (cfg4): configuration 4 as specified, 64 requests in
+  all, rank r owning requests r, r + N, ...;
+* ``runtime``: decode tokens/s of request-sharded serving through the runtime
+  harness, the NCCL all-gather of finished token ids inside the timed region.
+
+Every N runs under a process group (a single-rank one at N=1); times are
+taken on the device and reduced MAX over ranks, work is summed.  Rank 0
+prints one JSON line.  ``--impl reference`` times the reference algorithm's
+CPU restatement (oracle/: paged_attention_batch_online_v1, the SDPA v2
+prefill, the KV write loop of minivllm) on the host cores instead; under
+torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -78,32 +89,49 @@ def _tables(counts, perm):
 
 # ------------------------------------------------------------------ workloads
 class DecodeWorkload:
-    """Fused KV write + paged decode over one batch (configuration 4 or 3)."""
+    """Fused KV write + paged decode over one batch (configuration 4 or 3).
+
+    Weak scaling (default): every rank owns ``batch`` requests.  With
+    ``strong=True`` the batch is the global one and rank r owns requests
+    r, r + world, ... of it (configuration 4 as specified: 64 requests in
+    all, sharded by request).
+    """
 
     bound, unit = "hbm", "GB/s"
 
-    def __init__(self, name, rank, device, batch=None, ctx=None, kv_dtype="bf16"):
+    def __init__(self, name, rank, device, batch=None, ctx=None, kv_dtype="bf16",
+                 world=1, strong=False):
         self.name, self.device = name, device
         self.kv_name = kv_dtype
         self.dt = torch.float32 if kv_dtype == "f32" else torch.bfloat16
         self.es = 4 if kv_dtype == "f32" else 2
+        self.strong, self.world = strong, world
         if name == "cfg4":
-            self.B = batch or 64
-            lens = [ctx or 32768] * self.B
-            self.desc = (f"config 4: long-context split-K decode, {kv_dtype} KV, {self.B} requests/GPU"
-                         f" x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
+            self.global_B = batch or 64
+            lens = [ctx or 32768] * self.global_B
+            per = "in all" if strong else "per GPU"
+            self.desc = (f"config 4: long-context split-K decode, {kv_dtype} KV, {self.global_B}"
+                         f" requests {per} x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
         else:
-            self.B = batch or 256
-            g = torch.Generator().manual_seed(1000 + rank)
-            lens = torch.randint(1, 4097, (self.B,), generator=g).tolist()
+            self.global_B = batch or 256
+            # Configuration 3: contexts ~U[1, 4096] (seed 0), the first one 1
+            # and the last one forced to a non-multiple of the block size.
+            g = torch.Generator().manual_seed(0 if strong else rank)
+            lens = torch.randint(1, 4097, (self.global_B,), generator=g).tolist()
             lens[0] = 1
             if lens[-1] % S == 0:
                 lens[-1] -= 1
-            self.desc = (f"config 3: ragged decode, {kv_dtype} KV, batch {self.B}/GPU, contexts"
-                         " ~U[1,4096], H=32, D=128, S=16, fused KV write")
+            per = "in all" if strong else "per GPU"
+            self.desc = (f"config 3: ragged decode, {kv_dtype} KV, batch {self.global_B} {per},"
+                         " contexts ~U[1,4096], H=32, D=128, S=16, fused KV write")
+        if strong:
+            lens = lens[rank::world]
+        self.B = len(lens)
         self.lens = lens
         counts = [math.ceil(n / S) for n in lens]
-        P = sum(counts) + max(1, sum(counts) // 100)
+        # The pool holds the needed blocks plus 10 % spare (configuration 3's
+        # sizing; configuration 4 uses the same rule).
+        P = math.ceil(1.1 * sum(counts))
         g = torch.Generator(device=device).manual_seed(20260000 + rank)
         self.k = torch.empty((1, P, S, H, D), dtype=self.dt, device=device).normal_(generator=g)
         self.v = torch.empty_like(self.k).normal_(generator=g)
@@ -153,17 +181,21 @@ class DecodeWorkload:
         return self.out_h.numel() * self.out_h.element_size()
 
     def config(self, world):
-        return {"workload": self.desc, "batch_per_gpu": self.B, "global_batch": self.B * world,
+        glob = self.global_B if self.strong else self.B * world
+        return {"workload": self.desc, "batch_per_gpu": self.B, "global_batch": glob,
                 "context_lens": str(self.lens[0]) if self.name == "cfg4" else "U[1,4096]",
                 "heads": H, "head_dim": D, "block_size": S, "kv_dtype": self.kv_name,
                 "q_dtype": self.kv_name, "accumulate": "f32", "fused_kv_write": True,
                 "l2": "inputs larger than L2 (KV pool %.1f GB per GPU), no flush" % self.kv_gb,
                 "parallelism": f"request-sharded dp{world} (no data-path collective)"}
 
-    def extra(self, ms_max, world, steps):
-        value = self.work() * world * steps / (ms_max * 1e-3) / 1e9
+    def extra(self, value, ms_max, world, steps):
+        glob = self.global_B if self.strong else self.B * world
+        # One decode-attention launch serves one layer of one decode step of
+        # every request in the batch: this is a per-layer attention rate, not
+        # the runtime's decode tokens/s (that is the "runtime" object).
         return {"pct_of_8tbs": 100.0 * value / world / NOMINAL_HBM_GBS,
-                "decode_tokens_per_s": self.B * world * steps / (ms_max * 1e-3)}
+                "attention_launch_rows_per_s": glob * steps / (ms_max * 1e-3)}
 
 
 class PrefillWorkload:
@@ -235,7 +267,7 @@ class PrefillWorkload:
                 "l2": "KV pool %.1f GB per GPU (larger than L2), no flush" % self.kv_gb,
                 "parallelism": f"sequence-sharded dp{world}"}
 
-    def extra(self, ms_max, world, steps):
+    def extra(self, value, ms_max, world, steps):
         sec = ms_max * 1e-3 / steps
         return {"prefill_gbs": self.bytes() * world / sec / 1e9,
                 "prefill_tokens_per_s": self.nseq * self.T * world / sec}
@@ -287,7 +319,7 @@ class ScatterWorkload:
                 "l2": "each step moves %.0f MB; no flush between steps" % (self.work() / 1e6),
                 "parallelism": f"token-sharded dp{world}"}
 
-    def extra(self, ms_max, world, steps):
+    def extra(self, value, ms_max, world, steps):
         return {}
 
 
@@ -353,7 +385,7 @@ class QkvWorkload:
                 "l2": "weights %.0f MB, no flush between steps" % (3 * self.C * self.C * 2 / 1e6),
                 "parallelism": f"token-sharded dp{world}"}
 
-    def extra(self, ms_max, world, steps):
+    def extra(self, value, ms_max, world, steps):
         """The unfused sequence the kernel replaces, timed the same way:
         torch's bf16 matmul (cuBLAS) into a [T, 3C] tensor, then the
         slot-mapping scatter of its k and v thirds."""
@@ -387,9 +419,22 @@ class QkvWorkload:
         return {"unfused_comparison": res}
 
 
-def make_workload(name, rank, device, args):
-    if name in ("cfg4", "cfg3"):
-        return DecodeWorkload(name, rank, device, args.batch, args.ctx, args.kv_dtype)
+def make_workload(name, rank, device, args, extra=False):
+    """The workload of ``name``; ``extra`` builds it at its default size
+    (the sub-objects of the default run ignore --batch / --ctx / --kv-dtype)."""
+    if name in ("cfg4", "cfg3", "cfg3-f32"):
+        kv = "f32" if name == "cfg3-f32" else ("bf16" if extra else args.kv_dtype)
+        batch = None if extra else args.batch
+        ctx = None if extra else args.ctx
+        wl = DecodeWorkload(name.split("-")[0], rank, device, batch, ctx, kv)
+        if name.startswith("cfg3") and kv == "f32" and not extra:
+            wl.traffic_key = None
+        elif name.startswith("cfg3"):
+            wl.traffic_key = "cfg3" if kv == "bf16" and wl.B == 256 else None
+        else:
+            wl.traffic_key = "cfg4" if kv == "bf16" and wl.B == 64 and wl.lens[0] == 32768 \
+                else None
+        return wl
     if name == "cfg5-t512":
         return PrefillWorkload(512, rank, device)
     if name == "cfg5-t64":
@@ -397,7 +442,9 @@ def make_workload(name, rank, device, args):
     if name == "scatter":
         return ScatterWorkload(rank, device)
     if name in ("qkv-prefill", "qkv-decode"):
-        return QkvWorkload(name, rank, device)
+        wl = QkvWorkload(name, rank, device)
+        wl.traffic_key = name
+        return wl
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -416,7 +463,10 @@ class ClockSampler:
         self._t0, self._t1 = None, None
 
     def mark_start(self) -> None:
+        """Opens a new timed window (one per workload); summary() reports
+        the most recent one."""
         self._t0 = time.perf_counter()
+        self._t1 = None
 
     def mark_stop(self) -> None:
         self._t1 = time.perf_counter()
@@ -649,66 +699,176 @@ TRAFFIC_FILES = {"cfg4": "paged_decode_cfg4_traffic.json", "cfg3": "paged_decode
                  "qkv-decode": "qkv_kv_write_decode_traffic.json"}
 
 
-def traffic_from_profile(workload: str) -> float | None:
+def traffic_from_profile(workload: str | None, algorithmic: float) -> float | None:
+    """ncu DRAM bytes per launch of a workload at its full size, from the
+    committed profile summary, or None when none was captured for it.  A
+    summary holds either the full-size figure or the ratio of captured DRAM
+    bytes to algorithmic bytes (applied to this launch's algorithmic bytes)."""
     if workload not in TRAFFIC_FILES:
         return None
     p = REPO / "profiles" / TRAFFIC_FILES[workload]
     try:
-        return float(json.loads(p.read_text())["dram_bytes_per_launch_full_size"])
+        d = json.loads(p.read_text())
+        if "dram_over_algorithmic" in d:
+            return float(d["dram_over_algorithmic"]) * algorithmic
+        return float(d["dram_bytes_per_launch_full_size"])
     except Exception:
         return None
 
 
-def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+class RuntimeWorkload:
+    """Request-sharded serving through the runtime harness (decode tokens/s).
+
+    64 requests in all (1024-token prompts of random ids, 128 greedy outputs
+    each) over a random-init MiniGPT with 8 heads of 128 dims, 4 layers,
+    fp32 weights and KV, TF32 off; rank r serves requests r, r + N, ... with
+    its own scheduler, block manager and KV pool, device block tables and
+    CUDA-graph decode steps.  The timed region runs from the first request's
+    admission to the end of the NCCL all-gather of every rank's finished
+    token ids (b200attn.harness.sharded.serve_shard), on the device clock,
+    max over ranks.
+    """
+
+    def __init__(self, rank, world, device, requests=64, prompt=1024, output=128, heads=8,
+                 layers=4, vocab=256, block_size=16, token_budget=2048):
+        from b200attn.harness import MiniGPT, SequenceState, init_weights
+
+        self.rank, self.world, self.device = rank, world, device
+        self.requests, self.prompt, self.output = requests, prompt, output
+        self.heads, self.layers, self.block_size = heads, layers, block_size
+        self.token_budget = token_budget
+        torch.backends.cuda.matmul.allow_tf32 = False
+        self.model = MiniGPT(n_embd=heads * 128, n_head=heads, vocab_size=vocab,
+                             block_size=prompt + output + 1, n_layer=layers).eval()
+        init_weights(self.model, seed=0)
+        self.model.to(device)
+        g = torch.Generator().manual_seed(0)
+        prompts = [torch.randint(0, vocab, (prompt,), generator=g).tolist()
+                   for _ in range(requests)]
+        self.idx = list(range(requests))[rank::world]
+        self.local = [SequenceState(seq_id=f"r{i}", prompt_tokens=prompts[i],
+                                    max_tokens=prompt + output) for i in self.idx]
+        self.desc = (f"sharded runtime: {requests} requests in all x {prompt}-token prompts ->"
+                     f" {output} outputs, MiniGPT {heads} heads x 128 dims, {layers} layers, fp32,"
+                     " device block tables + CUDA-graph decode, NCCL all-gather of token ids")
+
+    def _runtime(self, n_local):
+        from b200attn.harness import build_runtime
+
+        per_req = -(-(self.prompt + self.output) // self.block_size)
+        rt = build_runtime(self.model, num_blocks=per_req * max(n_local, 1),
+                           block_size=self.block_size, max_running=max(n_local, 1),
+                           token_budget=self.token_budget, policy="conservative",
+                           n_head=self.heads, head_dim=128, device_tables=True, graphs=True)
+        rt.sync_cuda_timing = True
+        return rt
+
+    def run(self) -> dict:
+        import hashlib
+        import torch.distributed as dist
+        from b200attn.harness import SequenceState
+        from b200attn.harness.sharded import serve_shard
+
+        rt = self._runtime(len(self.local))
+        with torch.inference_mode():
+            rt.runner.graphs.capture_all()
+            # Warm-up: two short requests through the same runtime (cuBLAS
+            # handles, allocator); their blocks return to the free list.
+            warm = [SequenceState(seq_id=f"w{i}", prompt_tokens=[1 + i] * 40, max_tokens=48)
+                    for i in range(2)]
+            for r in warm:
+                rt.add_request(r)
+            rt.run_to_completion(warm)
+        rt.records.clear()
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        tokens, m = serve_shard(rt, self.local, self.idx, self.rank, self.world, self.device,
+                                status_timeout_s=120.0, tag="bench")
+        dec = [x for x in rt.records if x.decode_tokens > 0]
+        launches = sum(self.layers for x in rt.records if x.decode_tokens > 0) + \
+            sum(2 * self.layers * x.prefill_requests for x in rt.records)
+        local = torch.tensor([m["run_ms"] + m["gather_ms"], m["run_ms"], m["gather_ms"],
+                              sum(x.decode_ms for x in dec)], dtype=torch.float64,
+                             device=self.device)
+        counts = torch.tensor([m["output_tokens"], m["decode_tokens"], m["prefill_tokens"],
+                               launches], dtype=torch.float64, device=self.device)
+        dist.all_reduce(local, op=dist.ReduceOp.MAX)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM)
+        total_ms, run_ms, gather_ms, dec_ms = (float(x) for x in local)
+        out_tok, dec_tok, pre_tok, launches = (float(x) for x in counts)
+        digest = hashlib.sha256(json.dumps([tokens[i] for i in sorted(tokens)]).encode())
+        return {
+            "workload": self.desc,
+            "decode_tokens_per_s": dec_tok / (dec_ms * 1e-3) if dec_ms else None,
+            "output_tokens_per_s": out_tok / (total_ms * 1e-3),
+            "timed_ms": total_ms, "run_ms_max": run_ms, "gather_ms_max": gather_ms,
+            "decode_phase_ms_max": dec_ms, "output_tokens": out_tok, "decode_tokens": dec_tok,
+            "prefill_tokens": pre_tok, "requests_per_gpu": len(self.local),
+            "gpu_launches": int(launches),
+            "tokens_sha256": digest.hexdigest(), "requests_finished": len(tokens),
+            "timing": "device events on the serving stream, max over ranks; decode_phase_ms is"
+                      " the runtime's per-step decode phases (host clock around a device sync)",
+        }
+
+
+def _barrier(dist_on: bool) -> None:
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def time_workload(wl, args, dev, clocks) -> dict:
+    """Warm-up, K device-timed steps and K end-to-end steps of one workload;
+    the times are reduced MAX and the work SUM over ranks."""
     import torch.distributed as dist
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    pg = world > 1
-    if pg:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    wl = make_workload(args.workload, rank, dev, args)
     stream = torch.cuda.current_stream(dev)
-    with torch.inference_mode(), ClockSampler(gpu_indices(world)) as clocks:
-        wl.prepare()
-        for _ in range(args.warmup):
-            wl.step()
-        torch.cuda.synchronize(dev)
-        if pg:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        clocks.mark_start()
-        ev0.record(stream)
-        for _ in range(args.steps):
-            wl.step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-        clocks.mark_stop()
-        ms = ev0.elapsed_time(ev1)
-        if pg:
-            dist.barrier()
-        # End to end through the public API: H2D of the step's inputs from
-        # pinned memory, the call, D2H of the result, host synchronisation.
-        for _ in range(2):
-            wl.e2e_step()
+    wl.prepare()
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        wl.step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.mark_stop()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.summary()
+    dist.barrier()
+    # End to end through the public API: H2D of the step's inputs from pinned
+    # memory, the call, D2H of the result, a host synchronisation per step.
+    for _ in range(2):
+        wl.e2e_step()
+    stream.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        wl.e2e_step()
         stream.synchronize()
-        if pg:
-            dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            wl.e2e_step()
-            stream.synchronize()
-        e2e_s = time.perf_counter() - t0
-    times = torch.tensor([ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
-    if pg:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms_max, e2e_ms_max = float(times[0]), float(times[1])
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    work = torch.tensor([wl.work()], dtype=torch.float64, device=dev)
+    dist.all_reduce(work, op=dist.ReduceOp.SUM)
+    return {"ms": ms, "ms_max": float(times[0]), "e2e_ms_max": float(times[1]),
+            "work_sum": float(work[0]), "clocks": clk}
+
+
+def summarize(wl, r: dict, args, world: int) -> dict:
+    """The JSON fields of one timed workload."""
+    K = args.steps
     scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
-    value = wl.work() * world * args.steps / (ms_max * 1e-3) / scale
-    e2e_value = wl.work() * world * args.steps / (e2e_ms_max * 1e-3) / scale
-    per_launch_s = ms * 1e-3 / args.steps  # this rank's own kernel time
+    value = r["work_sum"] * K / (r["ms_max"] * 1e-3) / scale
+    e2e_value = r["work_sum"] * K / (r["e2e_ms_max"] * 1e-3) / scale
+    per_launch_s = r["ms"] * 1e-3 / K  # this rank's own kernel time
     if wl.bound == "tensor":
         peak, src = measured_peak("bf16_tflops")
         achieved, r_unit = wl.flops() / per_launch_s / 1e12, "TFLOP/s"
@@ -716,6 +876,82 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         peak, src = measured_peak("hbm_gbs")
         nbytes = wl.bytes() if hasattr(wl, "bytes") else wl.work()
         achieved, r_unit = nbytes / per_launch_s / 1e9, "GB/s"
+    return {
+        "value": value, "unit": wl.unit, "ms_per_step": r["ms_max"] / K,
+        "config": wl.config(world), **wl.extra(value, r["ms_max"], world, K),
+        "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
+                     "frac": achieved / peak, "peak_source": src,
+                     "traffic": traffic_from_profile(getattr(wl, "traffic_key", None), wl.work()),
+                     "algorithmic_per_launch": wl.work()},
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
+                "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": r["e2e_ms_max"] / K},
+        "clocks": r["clocks"], "gpu_launches": K,
+    }
+
+
+# The workloads the default run times besides the headline one, each reported
+# as a sub-object of the JSON line: configuration 3 (batch 256, bf16 and fp32
+# KV), configuration 5 (chunks 512 and 64), the prefill scatter and the fused
+# QKV projection at prefill and decode sizes.
+EXTRA_WORKLOADS = ("cfg3", "cfg3-f32", "cfg5-t512", "cfg5-t64", "scatter", "qkv-prefill",
+                   "qkv-decode")
+
+
+def _free(dev) -> None:
+    import gc
+    gc.collect()
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    # One process group at every N (a single-rank one at N=1), so that every
+    # N runs the same code: barriers, the MAX/SUM reductions of the timings
+    # and the runtime's NCCL token gather.
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    else:
+        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
+                                timeout=timedelta(seconds=180), device_id=dev)
+    with torch.inference_mode(), ClockSampler(gpu_indices(world)) as clocks:
+        wl = make_workload(args.workload, rank, dev, args)
+        head = summarize(wl, time_workload(wl, args, dev, clocks), args, world)
+        head_desc = wl.config(world)
+        del wl
+        _free(dev)
+        extras = {}
+        if not args.only:
+            if args.workload == "cfg4":
+                # Configuration 4 as specified: 64 requests in all, rank r
+                # owning requests r, r + N, ... (strong scaling).
+                if world > 1:
+                    wl = DecodeWorkload("cfg4", rank, dev, batch=args.batch, ctx=args.ctx,
+                                        kv_dtype=args.kv_dtype, world=world, strong=True)
+                    strong = summarize(wl, time_workload(wl, args, dev, clocks), args, world)
+                    del wl
+                    _free(dev)
+                else:
+                    strong = {k: head[k] for k in ("value", "unit", "ms_per_step", "e2e")}
+                    strong["same_as_headline"] = True
+                strong["scaling"] = "strong"
+                extras["strong_scaling"] = strong
+            for name in EXTRA_WORKLOADS:
+                if name == args.workload and args.kv_dtype == "bf16":
+                    continue
+                wl = make_workload(name, rank, dev, args, extra=True)
+                extras.setdefault("workloads", {})[name] = \
+                    summarize(wl, time_workload(wl, args, dev, clocks), args, world)
+                del wl
+                _free(dev)
+            rw = RuntimeWorkload(rank, world, dev)
+            extras["runtime"] = rw.run()
+            del rw
+            _free(dev)
     cpu = None
     # The CPU baseline is an N=1 figure (under torchrun the other ranks would
     # wait for it in the closing barrier).
@@ -727,27 +963,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         cpu["value_1_thread"] = one["value"]
         cpu["cpu_model"] = cpu_model()
     if rank == 0:
-        metric = metric_name(args.workload, wl.unit)
         line = {
-            "metric": metric, "value": value, "unit": wl.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": getattr(wl, "kv_name", "bf16"), "data": "synthetic", "config": wl.config(world),
-            **wl.extra(ms_max, world, args.steps),
-            "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
-                         "frac": achieved / peak, "peak_source": src,
-                         "traffic": traffic_from_profile(args.workload),
-                         "algorithmic_per_launch": wl.work()},
+            "metric": metric_name(args.workload, head["unit"]), "value": head["value"],
+            "unit": head["unit"], "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.kv_dtype if args.workload in ("cfg4", "cfg3")
+            else "bf16", "data": "synthetic", "config": head_desc,
+            **{k: v for k, v in head.items() if k not in ("value", "unit", "ms_per_step",
+                                                          "config")},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
-                    "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms_max / args.steps},
-            "clocks": clocks.summary(),
-            "gpu_launches": args.steps,
+            **extras,
         }
         print(json.dumps(line), flush=True)
-    if pg:
-        dist.barrier()
-        dist.destroy_process_group()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
@@ -761,6 +990,9 @@ def main():
                     choices=("cfg4", "cfg3", "cfg5-t512", "cfg5-t64", "scatter", "qkv-prefill",
                              "qkv-decode"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", action="store_true",
+                    help="time the named workload alone (no sub-workloads, strong-scaling or"
+                         " runtime objects)")
     ap.add_argument("--batch", type=int, default=None,
                     help="decode requests per GPU (default: the workload's; smaller for profiling)")
     ap.add_argument("--kv-dtype", choices=("bf16", "f32"), default="bf16",

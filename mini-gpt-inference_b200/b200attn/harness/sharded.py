@@ -32,6 +32,19 @@ from .sequence import SequenceState
 
 _STATUS_PREFIX = "b200attn/sharded/status"
 
+# Calls of run_sharded / serve_shard made so far by this process.  Every rank
+# makes the same calls in the same order, so the count names one call on all
+# ranks; it is folded into the status keys so that a later call never sees
+# the statuses an earlier call posted (a rank that dropped out of call 2
+# would otherwise look alive through its "ok" of call 1).
+_CALLS = 0
+
+
+def _call_tag(tag: str) -> str:
+    global _CALLS
+    _CALLS += 1
+    return f"{tag}#{_CALLS}"
+
 
 def shard(items: Sequence, rank: int, world: int) -> list:
     """The items a rank owns: rank, rank + world, rank + 2*world, ..."""
@@ -93,6 +106,67 @@ def gather_outputs(local: dict[int, list[int]], world: int, device: torch.device
     return out
 
 
+class _Clock:
+    """Phase timestamps: CUDA events on the device's current stream for a
+    CUDA device (the device's own clock), perf_counter on the CPU."""
+
+    def __init__(self, device: torch.device):
+        self.cuda = device.type == "cuda"
+        self.device = device
+        self.marks: list = []
+
+    def mark(self) -> None:
+        if self.cuda:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self.marks.append(ev)
+        else:
+            self.marks.append(time.perf_counter())
+
+    def ms(self, i: int, j: int) -> float:
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+            return self.marks[i].elapsed_time(self.marks[j])
+        return (self.marks[j] - self.marks[i]) * 1e3
+
+
+def serve_shard(rt, local: Sequence[SequenceState], idx: Sequence[int], rank: int, world: int,
+                device: torch.device, status_timeout_s: float = 60.0,
+                tag: str = "") -> tuple[dict[int, list[int]], dict]:
+    """Runs a built runtime over this rank's requests, then the status
+    handshake and the token all-gather.
+
+    local[i] is global request idx[i].  The returned metrics carry the
+    runtime's metrics_summary plus ``run_ms`` (requests added until the
+    last one finished) and ``gather_ms`` (status handshake and all-gather),
+    timed on the device for a CUDA device.
+    """
+    store = dist.distributed_c10d._get_default_store()
+    tag = _call_tag(tag)
+    clock = _Clock(device)
+    metrics: dict = {}
+    try:
+        clock.mark()
+        for r in local:
+            rt.add_request(r)
+        with torch.inference_mode():
+            rt.run_to_completion(list(local))
+        clock.mark()
+        metrics = dict(rt.metrics_summary())
+    except Exception as exc:
+        post_status(store, rank, False, f"{type(exc).__name__}: {exc}", tag)
+        raise
+    post_status(store, rank, True, tag=tag)
+    wait_statuses(store, world, status_timeout_s, tag)
+    tokens = gather_outputs({i: list(r.generated_tokens) for i, r in zip(idx, local)}, world,
+                            device)
+    clock.mark()
+    metrics["run_ms"] = clock.ms(0, 1)
+    metrics["gather_ms"] = clock.ms(1, 2)
+    metrics["wall_s"] = clock.ms(0, 2) / 1e3
+    return tokens, metrics
+
+
 def run_sharded(requests: Sequence[SequenceState], make_runtime: Callable[[list], object],
                 rank: int, world: int, device: torch.device, status_timeout_s: float = 60.0,
                 tag: str = "") -> tuple[dict[int, list[int]] | None, dict]:
@@ -102,29 +176,15 @@ def run_sharded(requests: Sequence[SequenceState], make_runtime: Callable[[list]
     add_request / run_to_completion / metrics_summary.  Returns (tokens by
     global request index on every rank, local metrics).
     """
-    store = dist.distributed_c10d._get_default_store()
     idx = list(range(len(requests)))[rank::world]
     local = [requests[i] for i in idx]
-    metrics: dict = {}
     try:
         rt = make_runtime(local)
-        for r in local:
-            rt.add_request(r)
-        t0 = time.perf_counter()
-        with torch.inference_mode():
-            rt.run_to_completion(local)
-        if device.type == "cuda":
-            torch.cuda.synchronize(device)
-        metrics = dict(rt.metrics_summary())
-        metrics["wall_s"] = time.perf_counter() - t0
     except Exception as exc:
-        post_status(store, rank, False, f"{type(exc).__name__}: {exc}", tag)
+        store = dist.distributed_c10d._get_default_store()
+        post_status(store, rank, False, f"{type(exc).__name__}: {exc}", _call_tag(tag))
         raise
-    post_status(store, rank, True, tag=tag)
-    wait_statuses(store, world, status_timeout_s, tag)
-    tokens = gather_outputs({i: list(r.generated_tokens) for i, r in zip(idx, local)}, world,
-                            device)
-    return tokens, metrics
+    return serve_shard(rt, local, idx, rank, world, device, status_timeout_s, tag)
 
 
 def _cfg2_main() -> None:

@@ -139,6 +139,9 @@ int sm_count() {
 }
 
 }  // namespace
+
+int validate_decode_args(const b200_decode_args_t& a) { return check_decode(a); }
+
 }  // namespace b200
 
 using namespace b200;

@@ -11,6 +11,10 @@ namespace b200 {
 
 using DecodeLaunch = b200_decode_args_t;
 
+// The host-side checks b200_paged_decode runs on its arguments (capi.cu):
+// B200_OK, or the status and message it would return.
+int validate_decode_args(const b200_decode_args_t& a);
+
 int launch_paged_decode(const DecodeLaunch& a, cudaStream_t stream);
 int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream);
 // tcgen05 prefill over `n` sequences sharing one pool (bf16, D in {64,128}).

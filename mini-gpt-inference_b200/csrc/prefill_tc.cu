@@ -54,9 +54,6 @@ namespace {
 constexpr int kMaxSeqs = 64;   // sequences per launch (host splits larger batches)
 constexpr int kMaxWork = 2048; // (sequence, query pair) items per launch
 constexpr int kThreads = 384;  // K producer, S issuer, two 4-warp softmax groups, V producer, P.V issuer
-// Every kPolyEvery-th exponential pair of P runs on the FMA pipes (0: all on
-// MUFU; measured fastest while MUFU is not the limiting unit).
-constexpr int kPolyEvery = 0;
 constexpr int kBM = 128;       // queries per query tile (two tiles per CTA)
 // Key-tile configurations.  BN = 64: S is double-buffered per query tile
 // (the MMAs of tile k+1 run during the softmax of tile k); used when the
@@ -112,31 +109,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// Base-2 exponential of a pair on the FMA pipes, so that part of the softmax
-// exponentials bypass the 16/clock/SM MUFU unit.  x is clamped to >= -125
-// (the result stays a normal float; the true value is below 2^-125 and
-// vanishes in the row sum and in bf16 P anyway).  Range reduction: adding
-// 1.5 * 2^23 rounds x to the nearest integer j (left in the low mantissa
-// bits of t) and leaves f = x - j in [-0.5, 0.5]; 2^f is a degree-3
-// polynomial fitted to 2^f on [-0.5, 0.5] by weighted least squares with
-// Lawson reweighting toward minimax (max relative error 7.5e-5, below the
-// 2^-8 rounding of bf16 P; exp2_poly_fit.py regenerates the coefficients);
-// j is added to the exponent field of the polynomial's bit pattern.
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -125.f);
-  x.y = fmaxf(x.y, -125.f);
-  const float2 one2 = make_float2(1.f, 1.f), mone2 = make_float2(-1.f, -1.f);
-  const float2 t = ffma2(x, one2, make_float2(12582912.f, 12582912.f));
-  const float2 jf = ffma2(t, one2, make_float2(-12582912.f, -12582912.f));
-  const float2 f = ffma2(jf, mone2, x);
-  float2 q = ffma2(make_float2(0.0551716648f, 0.0551716648f), f,
-                   make_float2(0.2426111251f, 0.2426111251f));
-  q = ffma2(q, f, make_float2(0.6932609677f, 0.6932609677f));
-  q = ffma2(q, f, make_float2(0.9999280572f, 0.9999280572f));
-  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
-}
-
 // max(a, b, c) in one instruction (three-input max, sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
@@ -173,15 +145,8 @@ __device__ __forceinline__ float p_pass(uint32_t srow, float scale, float neg_m,
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
       const float2 a = ffma2(make_float2(sv[cur][e], sv[cur][e + 1]), sc2, nm2);
-      float p0, p1;
-      if (kPolyEvery > 0 && (e >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) {
-        const float2 pp = ex2_poly2(a);  // this pair on the FMA pipes
-        p0 = pp.x;
-        p1 = pp.y;
-      } else {
-        p0 = ex2_approx(a.x);
-        p1 = ex2_approx(a.y);
-      }
+      float p0 = ex2_approx(a.x);
+      float p1 = ex2_approx(a.y);
       if (MASK) {
         p0 = c + e <= lim ? p0 : 0.f;
         p1 = c + e + 1 <= lim ? p1 : 0.f;
@@ -212,15 +177,8 @@ __device__ __forceinline__ float p_regs(const float* sv, uint32_t srow, float sc
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
       const float2 a = ffma2(make_float2(sv[c + e], sv[c + e + 1]), sc2, nm2);
-      float p0, p1;
-      if (kPolyEvery > 0 && (e >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) {
-        const float2 pp = ex2_poly2(a);  // this pair on the FMA pipes
-        p0 = pp.x;
-        p1 = pp.y;
-      } else {
-        p0 = ex2_approx(a.x);
-        p1 = ex2_approx(a.y);
-      }
+      float p0 = ex2_approx(a.x);
+      float p1 = ex2_approx(a.y);
       if (MASK) {
         p0 = c + e <= lim ? p0 : 0.f;
         p1 = c + e + 1 <= lim ? p1 : 0.f;

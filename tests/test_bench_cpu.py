@@ -54,9 +54,18 @@ def test_clock_summary_widens_a_window_shorter_than_the_period(bench):
 
 def test_roofline_traffic_comes_from_committed_profiles(bench):
     for wl in ("cfg4", "cfg3", "qkv-prefill", "qkv-decode"):
-        t = bench.traffic_from_profile(wl)
+        t = bench.traffic_from_profile(wl, 1e9)
         assert t is not None and t > 0, wl
-    assert bench.traffic_from_profile("scatter") is None
+    # configuration 3's summary is a DRAM/algorithmic ratio, applied per launch
+    assert bench.traffic_from_profile("cfg3", 2e9) == pytest.approx(
+        2 * bench.traffic_from_profile("cfg3", 1e9))
+    assert bench.traffic_from_profile("scatter", 1e9) is None
+    assert bench.traffic_from_profile(None, 1e9) is None
+
+
+def test_default_run_names_every_extra_workload(bench):
+    assert set(bench.EXTRA_WORKLOADS) == {"cfg3", "cfg3-f32", "cfg5-t512", "cfg5-t64", "scatter",
+                                          "qkv-prefill", "qkv-decode"}
 
 
 def test_usable_cpus_is_positive(bench):

@@ -171,3 +171,35 @@ def test_ops_are_inference_only():
         with pytest.raises(ValueError, match="CUDA"):
             paged_attention_batch_b200(torch.zeros(2, 2, 8), pool, torch.zeros(2, 1, dtype=torch.long),
                                        torch.ones(2, dtype=torch.long), 0)
+
+
+@pytest.mark.parametrize("entry", ["b200_paged_decode", "b200_paged_decode_no_alloc",
+                                   "b200_kv_scatter", "b200_chunked_prefill"])
+def test_pool_row_limit_boundary_without_gpu(entry):
+    """The kernels address pool rows (layer, block, slot) as 32-bit TMA
+    coordinates and element offsets; the host rejects pools of 2^31 or more
+    token rows before any CUDA call, and accepts 2^31 - 1 rows (the next
+    check that fails then is an unrelated one: null q / k pointers)."""
+    import ctypes
+    from b200attn import _lib
+
+    lib = _lib.load()
+    fn = getattr(lib, entry)
+    struct = {"b200_kv_scatter": _lib.ScatterArgs, "b200_chunked_prefill": _lib.PrefillArgs}.get(
+        entry, _lib.DecodeArgs)
+    for rows, over in (((1 << 31), True), ((1 << 31) - 16, False)):
+        a = struct()
+        # L * P * S rows with S = 16; the pointers are never dereferenced.
+        a.pool = _lib.KVPool(1 << 20, 2 << 20, 1, rows // 16, 16, 2, 64, _lib.DTYPE_BF16)
+        if struct is _lib.ScatterArgs:
+            a.num_tokens = 1
+        elif struct is _lib.PrefillArgs:
+            a.num_tokens, a.block_table_len = 1, 1
+        else:
+            a.batch, a.table_width = 1, 1
+        rc = fn(ctypes.byref(a), None)
+        msg = _lib.last_error(lib)
+        if over:
+            assert rc == _lib.ERR_UNSUPPORTED and "2^31 token rows" in msg, (entry, msg)
+        else:
+            assert rc == _lib.ERR_INVALID_ARGUMENT and "2^31" not in msg, (entry, msg)

@@ -56,6 +56,16 @@ def _worker(rank: int, world: int, port: int, mode: str, out_dir: str) -> None:
 
     result = {}
     try:
+        if mode == "drop_second":
+            # A first call that every rank completes; rank 1 then leaves
+            # before the second call.  Its "ok" from the first call must not
+            # count for the second.
+            reqs2 = [SequenceState(seq_id=r.seq_id, prompt_tokens=list(r.prompt_tokens),
+                                   max_tokens=r.max_tokens) for r in reqs]
+            run_sharded(reqs2, make_runtime, rank, world, torch.device("cpu"),
+                        status_timeout_s=5.0)
+            if rank == 1:
+                os._exit(0)
         tokens, metrics = run_sharded(reqs, make_runtime, rank, world, torch.device("cpu"),
                                       status_timeout_s=5.0)
         result = {"tokens": {f"r{i}": t for i, t in tokens.items()}, "metrics": metrics}
@@ -105,6 +115,12 @@ def test_rank_failure_is_reported(tmp_path):
 
 def test_vanished_rank_is_detected(tmp_path):
     out = _launch("vanish", tmp_path)
+    assert 1 not in out
+    assert "did not report" in out[0]["error"]
+
+
+def test_rank_leaving_before_a_second_call_is_detected(tmp_path):
+    out = _launch("drop_second", tmp_path)
     assert 1 not in out
     assert "did not report" in out[0]["error"]
 
