@@ -787,21 +787,22 @@ class RuntimeWorkload:
         dec = [x for x in rt.records if x.decode_tokens > 0]
         launches = sum(self.layers for x in rt.records if x.decode_tokens > 0) + \
             sum(2 * self.layers * x.prefill_requests for x in rt.records)
-        local = torch.tensor([m["run_ms"] + m["gather_ms"], m["run_ms"], m["gather_ms"],
+        local = torch.tensor([m["wall_s"] * 1e3, m["run_ms"], m["handshake_ms"], m["gather_ms"],
                               sum(x.decode_ms for x in dec)], dtype=torch.float64,
                              device=self.device)
         counts = torch.tensor([m["output_tokens"], m["decode_tokens"], m["prefill_tokens"],
                                launches], dtype=torch.float64, device=self.device)
         dist.all_reduce(local, op=dist.ReduceOp.MAX)
         dist.all_reduce(counts, op=dist.ReduceOp.SUM)
-        total_ms, run_ms, gather_ms, dec_ms = (float(x) for x in local)
+        total_ms, run_ms, handshake_ms, gather_ms, dec_ms = (float(x) for x in local)
         out_tok, dec_tok, pre_tok, launches = (float(x) for x in counts)
         digest = hashlib.sha256(json.dumps([tokens[i] for i in sorted(tokens)]).encode())
         return {
             "workload": self.desc,
             "decode_tokens_per_s": dec_tok / (dec_ms * 1e-3) if dec_ms else None,
             "output_tokens_per_s": out_tok / (total_ms * 1e-3),
-            "timed_ms": total_ms, "run_ms_max": run_ms, "gather_ms_max": gather_ms,
+            "timed_ms": total_ms, "run_ms_max": run_ms, "handshake_ms_max": handshake_ms,
+            "gather_ms_max": gather_ms,
             "decode_phase_ms_max": dec_ms, "output_tokens": out_tok, "decode_tokens": dec_tok,
             "prefill_tokens": pre_tok, "requests_per_gpu": len(self.local),
             "gpu_launches": int(launches),

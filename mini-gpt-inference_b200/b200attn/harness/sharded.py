@@ -138,8 +138,9 @@ def serve_shard(rt, local: Sequence[SequenceState], idx: Sequence[int], rank: in
 
     local[i] is global request idx[i].  The returned metrics carry the
     runtime's metrics_summary plus ``run_ms`` (requests added until the
-    last one finished) and ``gather_ms`` (status handshake and all-gather),
-    timed on the device for a CUDA device.
+    last one finished), ``handshake_ms`` (the status handshake: waiting for
+    every rank to finish) and ``gather_ms`` (the token all-gather), timed on
+    the device for a CUDA device.
     """
     store = dist.distributed_c10d._get_default_store()
     tag = _call_tag(tag)
@@ -158,12 +159,14 @@ def serve_shard(rt, local: Sequence[SequenceState], idx: Sequence[int], rank: in
         raise
     post_status(store, rank, True, tag=tag)
     wait_statuses(store, world, status_timeout_s, tag)
+    clock.mark()
     tokens = gather_outputs({i: list(r.generated_tokens) for i, r in zip(idx, local)}, world,
                             device)
     clock.mark()
     metrics["run_ms"] = clock.ms(0, 1)
-    metrics["gather_ms"] = clock.ms(1, 2)
-    metrics["wall_s"] = clock.ms(0, 2) / 1e3
+    metrics["handshake_ms"] = clock.ms(1, 2)  # waiting for the slowest rank to finish
+    metrics["gather_ms"] = clock.ms(2, 3)     # the all-gather itself
+    metrics["wall_s"] = clock.ms(0, 3) / 1e3
     return tokens, metrics
 
 
