@@ -221,10 +221,12 @@ B200_API int b200_chunked_prefill_batch(const b200_prefill_batch_args_t* args, v
  * b200_paged_decode, but args->workspace / workspace_bytes are ignored and
  * the split-K scratch is a static device array of
  * B200_NO_ALLOC_SCRATCH_BYTES held by every GPU that loads the library.
- * Calls needing more scratch are rejected with B200_ERR_UNSUPPORTED.  The
- * first call on a device looks up the array's address (make it before any
- * stream capture).  All calls share the array: calls that overlap on the
- * GPU race and must be serialised by the caller.
+ * Arguments are checked exactly as by b200_paged_decode first; calls needing
+ * more scratch are then rejected with B200_ERR_UNSUPPORTED.  The first call
+ * in a CUDA context looks up the array's address in that context (make it
+ * before any stream capture); a later context on the same device, e.g.
+ * after cudaDeviceReset, gets its own lookup.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
  */
 #define B200_NO_ALLOC_SCRATCH_BYTES (4u << 20)
 B200_API int b200_paged_decode_no_alloc(const b200_decode_args_t* args, void* stream);

@@ -338,72 +338,6 @@ struct PairCfg {
   static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area too small");
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-  uint32_t d;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
-  return d;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
-                   "memory");
-}
-
-// 2-D TMA load into this CTA's shared memory whose completion is counted on
-// an mbarrier of the pair (a shared::cluster address, here CTA 0's).
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
-                                                 int32_t c0, int32_t c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
-      "elect.sync rx|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrives (once each) on the barrier at this offset in both CTAs of the pair
-// when the MMAs issued so far have completed.
-__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
-      "elect.sync rx|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
-      "h"(static_cast<uint16_t>(3))
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
-      "elect.sync rx|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     qkv_kv_write_pair_kernel(const __grid_constant__ CUtensorMap tmx,
                              const __grid_constant__ CUtensorMap tmw, const QkvParams p) {
@@ -1114,6 +1048,16 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
 QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
+  if (m_tiles <= 2 && T > 64) {
+    // 65..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
+    // 256) beats split-K clusters once those tiles fit in one wave: at
+    // hidden 4096, 128 tokens take 25.0 us on single CTAs against 29.3 us
+    // split-K, and 256 tokens 31.0 us on CTA pairs against 47.0 us.
+    const int64_t single_tiles = ceil_div(3 * C, 128);
+    const int64_t pair_tiles = ceil_div(3 * C, kPairBN);
+    if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
+    if (m_tiles == 2 && pair_tiles <= num_sms / 2) return {QkvPlan::kPair, kPairBN, 1, kBM};
+  }
   if (m_tiles <= 2) {
     // Few tokens (decode): the weights dominate and are read once, at a
     // per-SM rate that TMA caps.  Pick the tile width and reduction split
@@ -1149,7 +1093,9 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   for (int bn : cand) {
     const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
     const int64_t cost = ceil_div(tiles, num_sms) * step_clocks(bn);
-    if (cost < best_cost) {
+    // On a tie the single-CTA tiles win: their last wave is fuller (384
+    // tokens at hidden 4096: 42.9 us against 51.4 us on CTA pairs).
+    if (cost <= best_cost) {
       best = {QkvPlan::kSingle, bn, 1, kBM};
       best_cost = cost;
     }

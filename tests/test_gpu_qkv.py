@@ -74,15 +74,17 @@ def _check_pool(c, y, status_bits=0):
     (5, 256, 8, 16, 1, 0),
     (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (split-K clusters)
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
-    (100, 1024, 8, 16, 1, 0),    # split-K over 16 k-steps
-    (129, 4096, 32, 16, 2, 1),   # two token tiles, the second ragged (128-wide tiles)
+    (100, 1024, 8, 16, 1, 0),    # single CTAs, 128-wide tiles, 16 k-steps
+    (129, 4096, 32, 16, 2, 1),   # CTA pairs; the second CTA holds one token
+    (128, 4096, 32, 16, 1, 0),   # single CTAs, 128-wide tiles, one wave
+    (256, 4096, 32, 16, 1, 0),   # CTA pairs, one wave
     (300, 512, 4, 16, 1, 0),     # single CTAs, 64-wide tiles
     (1000, 4096, 32, 16, 1, 0),  # prefill chunk (CTA pairs, 256 x 256 tiles)
     (600, 2048, 16, 16, 2, 1),   # CTA pairs; the second CTA of the last pair has no rows
-    (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step, 32-wide split tiles
+    (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step, ragged 128-wide tile
     (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
     (200, 3136, 49, 16, 1, 0),   # 3C = 36.75 x 256: ragged last output tile
-    (200, 4160, 65, 16, 1, 0),   # split-K, two token tiles
+    (200, 4160, 65, 16, 1, 0),   # CTA pairs, ragged last output tile
     (200, 6400, 50, 16, 1, 0),   # more tiles than SMs: single CTAs, 128-wide tiles, 3 waves
     (1000, 4160, 65, 16, 1, 0),  # CTA pairs, 3C = 48.75 tiles: ragged last output tile
 ])
@@ -234,8 +236,9 @@ def test_qkv_kv_write_full_size_against_cublas():
 
 
 @pytest.mark.parametrize("T,C,kind", [
-    (1, 4096, 2), (64, 4096, 2), (129, 4096, 2), (200, 6400, 0), (300, 512, 0),
-    (512, 4096, 1), (1000, 4096, 1), (8192, 4096, 1),
+    (1, 4096, 2), (64, 4096, 2), (100, 1024, 0), (128, 4096, 0), (129, 4096, 1),
+    (256, 4096, 1), (200, 6400, 0), (300, 512, 0), (384, 4096, 0), (512, 4096, 1),
+    (1000, 4096, 1), (8192, 4096, 1),
 ])
 def test_qkv_plan_covers_each_kernel(T, C, kind):
     """The shapes of the parity tests reach the kernel their comments name:
