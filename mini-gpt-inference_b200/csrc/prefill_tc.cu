@@ -89,7 +89,6 @@ struct PrefillParams {
   int32_t q_vec, out_vec;  // 16-byte row access is legal for every sequence
   int32_t q_tma;           // every sequence's q is bf16 and TMA-addressable
   int32_t rbox, rb_shift, s_shift;
-  int32_t rbox_v;          // V box rows of the CTA-pair kernel (min(S, 128))
   int32_t nseq;
   int32_t max_qtiles;
   int32_t* status;
@@ -758,494 +757,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-
-// ------------------------------------------------------------------ CTA pairs
-// Chunks longer than one query tile (head_dim 128, bf16 q read by TMA) run
-// as clusters of two CTAs.  A pair covers (sequence, head, 256 queries) and
-// CTA r holds query tile r (queries i0 + 128r .. i0 + 128r + 127).  CTA 0
-// issues the pair's tcgen05.mma.cta_group::2 instructions:
-//   S(j) = Q K(j)^T   M = 256 queries, N = 128 keys, K = 128 dims; CTA r
-//                     stages keys [64r, 64r + 64) of key tile j;
-//   O += P(j) V(j)    M = 256 queries, N = 128 dims, K = 128 keys; CTA r
-//                     stages dims [64r, 64r + 64) of all 128 keys, and P(j)
-//                     is read from each CTA's own TMEM.
-// Per SM this stages half the K/V bytes of a single-CTA tile, issues one MMA
-// per 16 keys x 256 queries, and the S MMA reads 6 KB of shared memory per
-// 64 clocks of math, within the 128 bytes/clock an SM's shared memory gives
-// (an N = 64, M = 128 MMA of a single CTA needs 6 KB per 32 clocks).
-// TMEM of each CTA: S buffers 0..2 at columns [0, 384) and O at [384, 512).
-// S(j) goes to buffer j % 3, so S(j+2) is issued right after P.V(j), and the
-// softmax of tile j+1 runs while the tensor core does P.V(j) and S(j+2).
-// Softmax: the 8 warps of each CTA pair up on TMEM lane quarters (warps
-// 2+q and 6+q read lanes 32q .. 32q+31); the two warps of a quarter split
-// each row's 128 key columns in halves and exchange their partial row
-// maxima once per tile through shared memory and an mbarrier.
-// The V ring starts zeroed and only blocks holding valid keys are loaded;
-// in the last tile, whose copies complete on a barrier of their own CTA,
-// the producer zeroes the rows of a partial block past the last key before
-// CTA 0 may read the tile.  So every V row the P.V MMA reads is finite:
-// P = 0 times a NaN from an unwritten pool row would be NaN.
-constexpr int kPairBN = 128;      // keys per tile
-constexpr int kPairKS = 5;        // K ring stages
-constexpr int kPairVS = 5;        // V ring stages
-struct PairSmem {
-  static constexpr int QHALF = kBM * 128;            // 128 queries x 64 dims
-  static constexpr int KHALF = 64 * 128;             // 64 keys x 64 dims
-  static constexpr int KSTAGE = 2 * KHALF;           // this CTA's 64 keys, 128 dims
-  static constexpr int VSTAGE = kPairBN * 128;       // 128 keys x this CTA's 64 dims
-  static constexpr int Q0 = 0;
-  static constexpr int K0 = Q0 + 2 * QHALF;
-  static constexpr int V0 = K0 + kPairKS * KSTAGE;
-  static constexpr int XCH = V0 + kPairVS * VSTAGE;  // [2 parities][2 halves][128 rows] floats
-  static constexpr int BAR = XCH + 2 * 2 * kBM * 4;
-  static constexpr int BYTES = BAR + 512;
-  static_assert(KSTAGE % 1024 == 0 && VSTAGE % 1024 == 0, "stages keep the swizzle alignment");
-};
-// TMEM columns of the pair kernel.
-constexpr uint32_t kPairOCol = 3 * kPairBN;
-
-// Row maximum of 64 raw scores (keys c <= lim only when MASK).
-template <bool MASK>
-__device__ __forceinline__ float row_max64(const float* sv, int lim) {
-  float mp[8];
-  if (MASK) {
-#pragma unroll
-    for (int a = 0; a < 8; ++a)
-      mp[a] = fmaxf(2 * a <= lim ? sv[2 * a] : -INFINITY, 2 * a + 1 <= lim ? sv[2 * a + 1] : -INFINITY);
-#pragma unroll
-    for (int e = 16; e < 64; e += 16)
-#pragma unroll
-      for (int a = 0; a < 8; ++a)
-        mp[a] = fmax3(mp[a], e + 2 * a <= lim ? sv[e + 2 * a] : -INFINITY,
-                      e + 2 * a + 1 <= lim ? sv[e + 2 * a + 1] : -INFINITY);
-  } else {
-#pragma unroll
-    for (int a = 0; a < 8; ++a) mp[a] = fmaxf(sv[2 * a], sv[2 * a + 1]);
-#pragma unroll
-    for (int e = 16; e < 64; e += 16)
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mp[a] = fmax3(mp[a], sv[e + 2 * a], sv[e + 2 * a + 1]);
-  }
-  return fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
-}
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    prefill_pair_kernel(const __grid_constant__ CUtensorMap tmk,
-                        const __grid_constant__ CUtensorMap tmv,
-                        const __grid_constant__ PrefillParams p) {
-  using L = PairSmem;
-  constexpr int D = 128;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const uint32_t item = p.work[blockIdx.y];
-  const int seq = static_cast<int>(item & 0xFFu);
-  const int qp = static_cast<int>(item >> 8);
-  const int h = blockIdx.x >> 1;
-  const SeqDesc& sd = p.seq[seq];
-  // The host lists only pairs with queries (i0 < T), and neither CTA of a
-  // pair returns early: the pair's MMAs and barriers involve both.
-  const int i0 = qp * 2 * kBM;
-  const int qlo = i0 + static_cast<int>(rank) * kBM;  // this CTA's first query
-  const int64_t prefix = sd.prefix;
-  const int64_t total = prefix + min(sd.T, i0 + 2 * kBM);  // keys any query of the pair sees
-  const int nkt = static_cast<int>((total + kPairBN - 1) / kPairBN);
-  // The last tile's V ends inside a block: its copies take the tail path.
-  const bool v_tail_partial = (total % p.rbox_v) != 0;
-
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::BAR);  // [KS] CTA 0's count both CTAs
-  uint64_t* k_empty = k_full + kPairKS;     // [KS] both CTAs (CTA 0's commits)
-  uint64_t* v_full = k_empty + kPairKS;     // [VS] CTA 0's count both CTAs
-  uint64_t* v_empty = v_full + kPairVS;     // [VS] both CTAs
-  uint64_t* s_full = v_empty + kPairVS;     // [3] per S buffer, both CTAs
-  uint64_t* p_full = s_full + 3;            // [3] per S buffer, CTA 0's: 8 warps x 2 CTAs
-  uint64_t* o_done = p_full + 3;            // P.V(j) complete = phase j, both CTAs
-  uint64_t* xbar = o_done + 1;              // [4 lane quarters][2 parities] max exchange
-  uint64_t* q_full = xbar + 8;              // CTA 0's: both Q tiles landed
-  uint64_t* mma_idle = q_full + 1;
-  uint64_t* v_tail = mma_idle + 1;          // this CTA's copies of a partial last V tile
-  uint64_t* v_tail_ready = v_tail + 1;      // CTA 0's: both CTAs zeroed that tile's tail
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_tail_ready + 1);
-  int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
-  volatile int32_t* abort_v = abort_flag;
-  static_assert((2 * kPairKS + 2 * kPairVS + 3 + 3 + 1 + 8 + 1 + 1 + 2) * 8 + 8 <= 512,
-                "barrier area too small");
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairKS; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-    }
-    for (int s = 0; s < kPairVS; ++s) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int b = 0; b < 3; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 16);
-    }
-    mbar_init(o_done, 1);
-    for (int x = 0; x < 8; ++x) mbar_init(&xbar[x], 64);
-    mbar_init(q_full, 1);
-    mbar_init(mma_idle, 1);
-    mbar_init(v_tail, 1);
-    mbar_init(v_tail_ready, 2);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  // The V ring starts zeroed (rows never loaded stay finite); the zeros are
-  // generic-proxy stores ordered before the ring's first TMA write.
-  for (int o = threadIdx.x * 16; o < kPairVS * L::VSTAGE; o += kThreads * 16)
-    *reinterpret_cast<uint4*>(smem + L::V0 + o) = make_uint4(0, 0, 0, 0);
-  fence_proxy_async_shared();
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(512)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  // Both CTAs' barriers exist before any copy, commit or arrival targets them.
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 || warp == 10) {
-    // ------------------------------------------------------------ producers (both CTAs)
-    // Warp 0 stages this CTA's 64 keys of each K tile (boxes {64 dims, 1
-    // head, min(S, 64) rows}, both dim halves), warp 10 this CTA's 64 dims
-    // of each V tile (boxes of min(S, 128) rows).  Every copy completes on
-    // CTA 0's stage barrier, whose expected byte count covers both CTAs'
-    // copies -- except those of a V tail tile (see v_tail).
-    const bool is_k = warp == 0;
-    const int NS = is_k ? kPairKS : kPairVS;
-    uint64_t* full = is_k ? k_full : v_full;
-    uint64_t* empty = is_k ? k_empty : v_empty;
-    const uint32_t full0 = map_to_rank(full, 0);
-    uint8_t* ring = smem + (is_k ? L::K0 : L::V0);
-    const int stage_bytes = is_k ? L::KSTAGE : L::VSTAGE;
-    const int rk = p.rbox;     // K rows per box
-    const int rv = p.rbox_v;   // V rows per box
-    if (is_k && lane == 0) {
-      // This CTA's Q tile (rows past T are zero-filled), on CTA 0's q_full.
-      if (rank == 0) mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(2 * 2 * L::QHALF));
-      const uint32_t qf0 = map_to_rank(q_full, 0);
-      for (int half = 0; half < 2; ++half)
-        tma_load_3d_pair(smem + L::Q0 + half * L::QHALF, &p.qmap[seq], qf0, half * 64, h, qlo);
-    }
-    int issued = 0;
-    for (int j = 0; j < nkt; ++j) {
-      const int st = j % NS;
-      const uint32_t use = static_cast<uint32_t>(j / NS);
-      const int64_t key0 = static_cast<int64_t>(j) * kPairBN;
-      // Boxes of this CTA (and, for CTA 0's byte count, of both CTAs).
-      int nbox = 0, vt = 0;
-      bool tail = false;
-      uint32_t pair_bytes = 0;
-      if (is_k) {
-        for (int rr = 0; rr < 2; ++rr) {
-          const int64_t left = total - (key0 + 64 * rr);
-          const int nb = static_cast<int>(min(static_cast<int64_t>(64 / rk),
-                                              max(static_cast<int64_t>(0), (left + rk - 1) / rk)));
-          pair_bytes += static_cast<uint32_t>(nb * 2 * rk * 128);
-          if (rr == static_cast<int>(rank)) nbox = 2 * nb;
-        }
-      } else {
-        vt = static_cast<int>(min(static_cast<int64_t>(kPairBN), total - key0));
-        tail = v_tail_partial && j == nkt - 1;
-        nbox = (vt + rv - 1) / rv;  // a partial block is loaded whole, its tail zeroed below
-        pair_bytes = static_cast<uint32_t>(2 * vt * 128);
-      }
-      // Block-table reads for this lane's box start before the slot wait.
-      const int b = is_k ? lane >> 1 : lane;
-      const int half = is_k ? lane & 1 : static_cast<int>(rank);
-      const bool mine = lane < nbox;
-      const int64_t key = is_k ? key0 + 64 * rank + static_cast<int64_t>(b) * rk
-                               : key0 + static_cast<int64_t>(b) * rv;
-      int64_t phys = 0;
-      if (mine) {
-        const int64_t blk = key >> p.s_shift;
-        phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
-        if (phys < 0 || phys >= p.P) {
-          report(p.status, B200_DEV_BAD_BLOCK);
-          phys = 0;
-        }
-      }
-      int ok = 1;
-      if (lane == 0) ok = (*abort_v == 0 && mbar_wait(&empty[st], (use & 1u) ^ 1u)) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) {
-          report(p.status, B200_DEV_WAIT_TIMEOUT);
-          *abort_flag = 1;
-        }
-        break;
-      }
-      if (lane == 0) {
-        if (tail)  // the tail tile's copies complete on this CTA's own barrier
-          mbar_arrive_expect_tx(v_tail, static_cast<uint32_t>(nbox * rv * 128));
-        else if (rank == 0)
-          mbar_arrive_expect_tx(&full[st], pair_bytes);
-      }
-      __syncwarp();
-      uint8_t* stage = ring + st * stage_bytes;
-      const uint32_t bar = full0 + static_cast<uint32_t>(st * 8);
-      if (mine) {
-        const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
-        if (is_k)
-          tma_load_3d_pair(stage + half * L::KHALF + b * rk * 128, &tmk, bar, half * 64, h, row);
-        else if (tail)
-          tma_load_3d(stage + b * rv * 128, &tmv, v_tail, half * 64, h, row);
-        else
-          tma_load_3d_pair(stage + b * rv * 128, &tmv, bar, half * 64, h, row);
-      }
-      if (tail) {
-        // Zero the rows of the partial block past the last key (unwritten
-        // pool rows may hold NaN), then tell CTA 0 this CTA's half is ready.
-        int got = 1;
-        if (lane == 0) got = mbar_wait(v_tail, 0) ? 1 : 0;
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-          if (lane == 0) {
-            report(p.status, B200_DEV_WAIT_TIMEOUT);
-            *abort_flag = 1;
-          }
-          break;
-        }
-        for (int o = vt * 128 + lane * 16; o < nbox * rv * 128; o += 32 * 16)
-          *reinterpret_cast<uint4*>(stage + o) = make_uint4(0, 0, 0, 0);
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(map_to_rank(v_tail_ready, 0));
-      }
-      ++issued;
-    }
-    // CTA 0 sees every copy of the pair land before the CTAs may exit.
-    if (rank == 0 && lane == 0) {
-      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
-        if (!(!is_k && v_tail_partial && j == nkt - 1) &&  // (waited on v_tail above)
-            !mbar_wait(&full[j % NS], static_cast<uint32_t>(j / NS) & 1u)) {
-          report(p.status, B200_DEV_WAIT_TIMEOUT);
-          break;
-        }
-      if (is_k && !mbar_wait(q_full, 0)) report(p.status, B200_DEV_WAIT_TIMEOUT);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (CTA 0)
-    // Order: S(0), S(1), then for every tile k: P.V(k) once P(k) is written
-    // in both CTAs, then S(k+2) into the buffer P(k-1) used (P.V(k-1) is
-    // complete: waited before P.V(k)).  S(k+2) is issued only after every
-    // softmax warp has written P(k), so no warp runs more than one tile
-    // ahead of another: o_done is then never two phases ahead of a warp
-    // that waits on it (a parity wait could not tell those phases apart).
-    if (rank == 0) {
-      auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-        return __all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(bar, parity)) != 0;
-      };
-      constexpr uint32_t idesc_s = idesc_bf16(2 * kBM, kPairBN, false);
-      constexpr uint32_t idesc_o = idesc_bf16(2 * kBM, D, true);
-      const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::Q0), 16, 1024);
-      const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::K0), 16, 1024);
-      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::V0), L::VSTAGE, 1024);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kPairKS;
-        if (!wait_all(&k_full[st], static_cast<uint32_t>(j / kPairKS) & 1u)) return false;
-        tc_fence_after();
-        const uint64_t dk = dk0 + static_cast<uint64_t>((st * L::KSTAGE) >> 4);
-        const uint32_t ts = tmem + static_cast<uint32_t>((j % 3) * kPairBN);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t qoff = static_cast<uint64_t>(((kk >> 2) * L::QHALF + (kk & 3) * 32) >> 4);
-          const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::KHALF + (kk & 3) * 32) >> 4);
-          mma_bf16_pair(ts, dq0 + qoff, dk + koff, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        mma_commit_pair_both(&s_full[j % 3]);
-        mma_commit_pair_both(&k_empty[st]);
-        return true;
-      };
-      bool ok = wait_all(q_full, 0);
-      for (int j = 0; ok && j < min(2, nkt); ++j) ok = issue_s(j);
-      for (int k = 0; ok && k < nkt; ++k) {
-        if (k >= 1 && !wait_all(o_done, static_cast<uint32_t>(k - 1) & 1u)) {
-          ok = false;
-          break;
-        }
-        if (!wait_all(&p_full[k % 3], static_cast<uint32_t>(k / 3) & 1u)) {
-          ok = false;
-          break;
-        }
-        const int vst = k % kPairVS;
-        const bool vtail = v_tail_partial && k == nkt - 1;
-        if (!(vtail ? wait_all(v_tail_ready, 0)
-                    : wait_all(&v_full[vst], static_cast<uint32_t>(k / kPairVS) & 1u))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t tp = tmem + static_cast<uint32_t>((k % 3) * kPairBN);
-        const uint64_t dv = dv0 + static_cast<uint64_t>((vst * L::VSTAGE) >> 4);
-        // P (bf16 pairs over S's first 64 columns) is the TMEM A operand:
-        // 16 keys per MMA = 8 columns; V advances 16 rows = 2048 bytes.
-#pragma unroll
-        for (int kk = 0; kk < kPairBN / 16; ++kk)
-          mma_bf16_pair_ts(tmem + kPairOCol, tp + kk * 8, dv + static_cast<uint64_t>(kk * 128),
-                           idesc_o, (k > 0 || kk > 0) ? 1u : 0u);
-        mma_commit_pair_both(o_done);
-        mma_commit_pair_both(&v_empty[vst]);
-        if (k + 2 < nkt) ok = issue_s(k + 2);
-      }
-      if (!ok && lane == 0) {
-        report(p.status, B200_DEV_WAIT_TIMEOUT);
-        *abort_flag = 1;
-      }
-      // Every MMA of the pair has completed before TMEM is freed.
-      mma_commit_pair_local(mma_idle);
-      if (!__all_sync(0xffffffffu, mbar_wait(mma_idle, 0)) && lane == 0)
-        report(p.status, B200_DEV_WAIT_TIMEOUT);
-    }
-  } else if (warp >= 2 && warp <= 9) {
-    // ------------------------------------------------------------ softmax (both CTAs)
-    const int q4 = warp & 3;            // TMEM lane quarter
-    const int ch = (warp - 2) >> 2;     // key-column half (and O dim half) of this warp
-    const int r = q4 * 32 + lane;       // row of this CTA's query tile = TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
-    const int iq = qlo + r;
-    const int i = min(iq, sd.T - 1);    // rows past T mirror the last query
-    const int64_t qpos = prefix + i;
-    // A quarter whose 32 rows are all past T computes nothing (both of its
-    // warps skip alike); it only keeps the barrier protocol.
-    const bool warp_live = qlo + q4 * 32 < sd.T;
-    const uint32_t p_full0 = map_to_rank(p_full, 0);
-    float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [parity][half][row]
-    uint64_t* qbar = xbar + 2 * q4;                        // this quarter's exchange barriers
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    int nx = 0;  // exchanges done (phase counter of qbar[nx & 1])
-    // Exchanges one float with the other warp of the quarter (same row).
-    auto exchange = [&](float mine) -> float {
-      xch[((nx & 1) * 2 + ch) * kBM + r] = mine;
-      mbar_arrive(&qbar[nx & 1]);
-      const bool got = mbar_wait(&qbar[nx & 1], static_cast<uint32_t>(nx >> 1) & 1u);
-      const float other = xch[((nx & 1) * 2 + (ch ^ 1)) * kBM + r];
-      ++nx;
-      if (!got) ok = false;
-      return other;
-    };
-    for (int k = 0; k < nkt; ++k) {
-      const int b = k % 3;
-      if (!mbar_wait(&s_full[b], static_cast<uint32_t>(k / 3) & 1u)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int64_t c0 = static_cast<int64_t>(k) * kPairBN + ch * 64;  // key of column 0
-      const bool need_mask = c0 + 63 > prefix + qlo;  // some key may be past some row's query
-      const int lim = static_cast<int>(max(min(qpos - c0, static_cast<int64_t>(63)),
-                                           static_cast<int64_t>(-1)));
-      float alpha = 1.f;
-      bool rescale = false;
-      if (warp_live) {
-        float sv[64];
-        const uint32_t srow = tmem + lane_base + static_cast<uint32_t>(b * kPairBN + ch * 64);
-        tmem_ld32(srow, sv);
-        tmem_ld32(srow + 32, sv + 32);
-        tmem_wait_ld();
-        float mx = (need_mask ? row_max64<true>(sv, lim) : row_max64<false>(sv, lim)) *
-                   p.scale_log2;
-        // Both warps have read their S columns before either writes P over
-        // columns [0, 64) of the buffer (the exchange orders them).
-        mx = fmaxf(mx, exchange(mx));
-        if (!ok) break;
-        // Lazy rescale: keep the old max unless the new one exceeds it by
-        // more than 8 (probabilities stay below 2^8).  Both warps of the
-        // quarter compute the same m_use from the same inputs.
-        const float m_use = mx > m + 8.f ? mx : m;
-        rescale = __any_sync(0xffffffffu, m_use != m) && k > 0;
-        alpha = m_use == m ? 1.f : ex2_approx(m - m_use);
-        const uint32_t prow = tmem + lane_base + static_cast<uint32_t>(b * kPairBN + ch * 32);
-        const float rsum = need_mask ? p_regs<true, 64>(sv, prow, p.scale_log2, -m_use, lim)
-                                     : p_regs<false, 64>(sv, prow, p.scale_log2, -m_use, lim);
-        l = l * alpha + rsum;
-        m = m_use;
-      }
-      if (rescale) {
-        // P.V(k-1) has completed before this warp's half of O is rescaled.
-        if (!mbar_wait(o_done, static_cast<uint32_t>(k - 1) & 1u)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 64; c += 32) {
-          float o[32];
-          const uint32_t oa = tmem + lane_base + kPairOCol + static_cast<uint32_t>(ch * 64 + c);
-          tmem_ld32(oa, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= alpha;
-          tmem_st32(oa, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote_tc(p_full0 + static_cast<uint32_t>(b * 8));
-    }
-    if (ok && !mbar_wait(o_done, static_cast<uint32_t>(nkt - 1) & 1u)) ok = false;
-    if (!ok) {
-      if (lane == 0) report(p.status, B200_DEV_WAIT_TIMEOUT);
-      *abort_flag = 1;
-    }
-    if (warp_live && ok) {
-      // Row sum = the two halves' partial sums; each warp writes its 64
-      // output dims.
-      const float lt = l + exchange(l);
-      if (ok) {
-        tc_fence_after();
-        const float inv = 1.0f / lt;
-        const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
-#pragma unroll
-        for (int c = 0; c < 64; c += 32) {
-          float o[32];
-          tmem_ld32(tmem + lane_base + kPairOCol + static_cast<uint32_t>(ch * 64 + c), o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= inv;
-          if (iq < sd.T) {
-            const int64_t base = iq * sd.os0 + h * sd.os1 + (ch * 64 + c) * sd.os2;
-            if (vec) {
-#pragma unroll
-              for (int e = 0; e < 32; e += 8) {
-                const uint4 wv = make_uint4(pack_bf16(o[e], o[e + 1]), pack_bf16(o[e + 2], o[e + 3]),
-                                            pack_bf16(o[e + 4], o[e + 5]), pack_bf16(o[e + 6], o[e + 7]));
-                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(sd.out) + base + e) = wv;
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) store_elem(sd.out, base + e * sd.os2, p.out_dtype, o[e]);
-            }
-          }
-        }
-      }
-    }
-  }
-  // Neither CTA frees TMEM or exits while the pair's MMAs, copies or
-  // arrivals may still touch it (every wait above is bounded, so both CTAs
-  // get here).
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
-                 : "memory");
-  }
-}
-
 }  // namespace
 
 bool prefill_tc_supported(const b200_prefill_args_t& a) {
@@ -1255,12 +766,9 @@ bool prefill_tc_supported(const b200_prefill_args_t& a) {
   return true;
 }
 
-// PAIR: sub-batches whose q is TMA-addressable run the CTA-pair kernel
-// (D_ == 128, BN == 64 for the fallback), the others prefill_tc_kernel.
-template <int D_, int BN, bool PAIR = false>
+template <int D_, int BN>
 int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
               const DeviceInfo& dev) {
-  static_assert(!PAIR || (D_ == 128 && BN == 64), "the pair kernel serves head_dim 128");
   int rc = B200_OK;
   const b200_prefill_args_t& a0 = seqs[0];
   const int64_t D = a0.pool.head_dim, H = a0.pool.num_heads, S = a0.pool.block_size;
@@ -1281,18 +789,6 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
   rc = encode_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a0.pool.v, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != B200_OK) return rc;
-  // The pair kernel's V map: boxes of min(S, 128) rows.
-  const int64_t rbox_v = std::min<int64_t>(S, kPairBN);
-  const size_t smem_pair = static_cast<size_t>(PairSmem::BYTES) + 1024;
-  CUtensorMap tvp;
-  if (PAIR) {
-    if (smem_pair > static_cast<size_t>(dev.max_smem_optin))
-      return fail(B200_ERR_UNSUPPORTED, "tensor-core prefill: not enough shared memory");
-    const uint32_t boxv[3] = {64u, 1u, static_cast<uint32_t>(rbox_v)};
-    rc = encode_tensor_map(&tvp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a0.pool.v, dims, strides,
-                           boxv, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != B200_OK) return rc;
-  }
 
   static std::atomic<int> configured[64];
   static std::mutex mu;
@@ -1303,11 +799,6 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
-    if (PAIR) {
-      e = cudaFuncSetAttribute(prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(smem_pair));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_pair)");
-    }
     configured[dev.device].store(1, std::memory_order_release);
   }
 
@@ -1326,7 +817,6 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
     prm.rbox = static_cast<int32_t>(rbox);
     prm.rb_shift = log2i(rbox);
     prm.s_shift = log2i(S);
-    prm.rbox_v = static_cast<int32_t>(rbox_v);
     prm.nseq = static_cast<int32_t>(cnt);
     prm.status = a0.status;
     prm.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(D)));
@@ -1399,8 +889,7 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
         for (int w = 0; w < 2; ++w) {
           const int64_t lo = qp * 2 * kBM + w * kBM;
           if (lo < s.num_tokens)
-            tiles += ceil_div(s.prefix_len + std::min<int64_t>(s.num_tokens, lo + kBM),
-                              PAIR ? kPairBN : BN);
+            tiles += ceil_div(s.prefix_len + std::min<int64_t>(s.num_tokens, lo + kBM), BN);
         }
         items.emplace_back(tiles, static_cast<uint32_t>(i) | (static_cast<uint32_t>(qp) << 8));
       }
@@ -1410,14 +899,8 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
     for (size_t w0 = 0; w0 < items.size(); w0 += kMaxWork) {
       const size_t nw = std::min<size_t>(kMaxWork, items.size() - w0);
       for (size_t k = 0; k < nw; ++k) prm.work[k] = items[w0 + k].second;
-      if (PAIR && prm.q_tma) {
-        // Clusters of two CTAs along x: CTA 2h + r is query tile r of head h.
-        const dim3 grid(static_cast<unsigned>(2 * H), static_cast<unsigned>(nw));
-        prefill_pair_kernel<<<grid, kThreads, smem_pair, stream>>>(tk, tvp, prm);
-      } else {
-        const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw));
-        prefill_tc_kernel<D_, BN><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
-      }
+      const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw));
+      prefill_tc_kernel<D_, BN><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "prefill_tc launch");
     }

@@ -195,39 +195,9 @@ __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
       : "memory");
 }
 
-// Arrival on a peer CTA's mbarrier with the default (CTA-scope) release:
-// enough to publish tcgen05 operations ordered by
-// tcgen05.fence::before_thread_sync, without the cluster-scope fence of
-// mbar_arrive_remote (which orders this thread's generic memory writes too).
-__device__ __forceinline__ void mbar_arrive_remote_tc(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
-}
-
-// Same as tma_load_2d_pair for a 3-D tensor map.
-__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
-                                                 int32_t c0, int32_t c1, int32_t c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-// Pair MMA with the A operand (each CTA's own 128 rows) in TMEM.
-__device__ __forceinline__ void mma_bf16_pair_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
-                                                 uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t"
-      "elect.sync rx|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 // Two floats -> one bf16 pair (round to nearest even), element 0 in the low half.
