@@ -780,6 +780,11 @@ class RuntimeWorkload:
                 rt.add_request(r)
             rt.run_to_completion(warm)
         rt.records.clear()
+        # One untimed all-gather of the timed one's shape: NCCL sets up a
+        # collective's connections on its first use, a one-time cost that
+        # is not the steady-state gather.
+        from b200attn.harness.sharded import gather_outputs
+        gather_outputs({i: [0] * self.output for i in self.idx}, self.world, self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier()
         tokens, m = serve_shard(rt, self.local, self.idx, self.rank, self.world, self.device,
