@@ -392,25 +392,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b = lane / L::HALVES;
     const int half = lane % L::HALVES;
     int issued = 0;
+    // Block-table entries are read one tile ahead: the load for tile j+1 is
+    // issued before tile j's slot wait, and an entry is checked only when it
+    // is used, so the load's latency overlaps the wait and the copies.
+    auto boxes = [&](int j) {
+      return static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
+                                  (g.total - static_cast<int64_t>(j) * kBN + p.rbox - 1) >> p.rb_shift));
+    };
+    auto entry = [&](int j) -> int64_t {
+      if (j >= g.nmax || lane >= boxes(j) * L::HALVES) return 0;
+      const int64_t blk = (static_cast<int64_t>(j) * kBN + (static_cast<int64_t>(b) << p.rb_shift)) >> p.s_shift;
+      return blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
+    };
+    int64_t raw_next = entry(0);
     for (int j = 0; j < g.nmax; ++j) {
       const int st = j % NS;
       const uint32_t use = static_cast<uint32_t>(j / NS);
       const int64_t key0 = static_cast<int64_t>(j) * kBN;
-      const int nb = static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
-                                          (g.total - key0 + p.rbox - 1) >> p.rb_shift));
-      // The block-table read does not depend on the ring slot: start it
-      // before waiting for the slot so its latency overlaps the wait.
+      const int nb = boxes(j);
       const bool mine = lane < nb * L::HALVES;
       const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
-      const int64_t blk = key >> p.s_shift;
-      int64_t phys = 0;
-      if (mine) {
-        phys = blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
-        if (phys < 0 || phys >= p.P) {
-          report(p.status, B200_DEV_BAD_BLOCK);
-          phys = 0;
-        }
-      }
+      const int64_t raw = raw_next;
+      raw_next = entry(j + 1);
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&empty[st], (use & 1u) ^ 1u) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -424,6 +427,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0)
         mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * L::HALVES * box_bytes));
       __syncwarp();
+      int64_t phys = raw;
+      if (mine && (phys < 0 || phys >= p.P)) {
+        report(p.status, B200_DEV_BAD_BLOCK);
+        phys = 0;
+      }
       if (mine) {
         uint8_t* dst = ring + st * L::KVTILE;
         const int32_t row = static_cast<int32_t>((p.layer * p.P + phys) * p.S + (key & (p.S - 1)));
