@@ -427,10 +427,10 @@ def make_workload(name, rank, device, args, extra=False):
         batch = None if extra else args.batch
         ctx = None if extra else args.ctx
         wl = DecodeWorkload(name.split("-")[0], rank, device, batch, ctx, kv)
-        if name.startswith("cfg3") and kv == "f32" and not extra:
-            wl.traffic_key = None
-        elif name.startswith("cfg3"):
-            wl.traffic_key = "cfg3" if kv == "bf16" and wl.B == 256 else None
+        # ncu traffic: configuration 3's captured DRAM/algorithmic ratio (bf16
+        # KV, any batch); configuration 4's full-size bytes (its default shape).
+        if name.startswith("cfg3"):
+            wl.traffic_key = "cfg3" if kv == "bf16" else None
         else:
             wl.traffic_key = "cfg4" if kv == "bf16" and wl.B == 64 and wl.lens[0] == 32768 \
                 else None
