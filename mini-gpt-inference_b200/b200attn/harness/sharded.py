@@ -62,6 +62,10 @@ def wait_statuses(store, world: int, timeout_s: float, tag: str = "") -> None:
     keys = [f"{_STATUS_PREFIX}{tag}/{r}" for r in range(world)]
     deadline = time.monotonic() + timeout_s
     missing = list(range(world))
+    # The poll interval starts at 0.5 ms and grows to 20 ms: ranks of a
+    # balanced shard finish within a few ms of each other, and every ms one
+    # rank oversleeps here delays every rank's all-gather that follows.
+    pause = 0.0005
     while missing and time.monotonic() < deadline:
         still = []
         for r in missing:
@@ -73,7 +77,8 @@ def wait_statuses(store, world: int, timeout_s: float, tag: str = "") -> None:
                 still.append(r)
         missing = still
         if missing:
-            time.sleep(0.05)
+            time.sleep(pause)
+            pause = min(0.02, pause * 1.5)
     if missing:
         raise RuntimeError(f"ranks {missing} did not report within {timeout_s:.1f} s")
 

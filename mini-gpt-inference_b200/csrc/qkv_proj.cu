@@ -555,11 +555,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // accumulates k-steps [r * kpb, +kpb) of one output tile in its own TMEM.
 // The x box is only as tall as the live tokens (rows of the A operand past
 // it hold stale data, which only reaches accumulator rows that are never
-// stored).  Each CTA stages its partial rows (live tokens only) in its
-// shared memory; CTA r then sums tokens r, r + splits, ... over the
-// cluster's staging areas in rank order (the same order every run), rounds
-// once to bf16 and stores them; the (token, 4-column group) items are spread
-// over all of the CTA's threads, several loads in flight per thread.
+// stored).  The live token rows are divided into `splits` contiguous
+// ranges of `per` rows, CTA r owning range r.  Once every CTA of the
+// cluster has its accumulator (a cluster barrier: every ring is idle),
+// each thread reads its TMEM row and writes it to the row's owner: into
+// its own staging rows, or with st.async into the owner's receive slot for
+// this CTA, completing as transaction bytes on the owner's recv_full
+// barrier.  The owner then sums its rows' partials in rank order (the same
+// order every run) from its own shared memory, rounds once to bf16 and
+// stores 32-column runs; the (row, run) items are spread over all of the
+// CTA's threads.  The slot of each owned row is read while the MMAs run.
 constexpr int kSplitMaxBN = 256;
 // A stage holds kc (1 or 2) consecutive 64-column chunks of x and W,
 // fetched by one 3-D box per operand ({64 columns, rows, chunks}; the chunk
@@ -568,11 +573,21 @@ constexpr int kSplitMaxBN = 256;
 // chunk keeps the ring at >= 3 stages when the x rows are many.
 constexpr int kSplitMaxKC = 2;
 constexpr int kSplitMaxStages = 24;
-constexpr int kSplitBarOffset = kRingBytes;          // barriers after the ring
-constexpr int kSplitBytes = kSplitBarOffset + 512;
-constexpr int kStageRowWords = kSplitMaxBN + 4;      // padded: 16-byte stores of a warp hit distinct banks
-static_assert(kBM * kStageRowWords * 4 <= kRingBytes, "staging must fit in the operand ring");
-static_assert((2 * kSplitMaxStages + 2) * 8 + 8 <= 512, "barrier area too small");
+// The operand ring, reused for the reduction rows once the MMAs are done;
+// then the barriers and the slot of each token row.
+constexpr int kSplitAreaBytes = 224 * 1024;
+constexpr int kSplitBarOffset = kSplitAreaBytes;
+constexpr int kSplitSlotOffset = kSplitBarOffset + 512;
+constexpr int kSplitBytes = kSplitSlotOffset + kBM * 8;
+static_assert((2 * kSplitMaxStages + 3) * 8 + 8 <= 512, "barrier area too small");
+
+// Bytes of the reduction area for `rows` live token rows: this CTA's own
+// rows, then a receive slot per peer, ceil(rows / splits) rows each.  Rows
+// are bn + 4 floats apart: 16-byte aligned, and the 16-byte accesses of a
+// warp's 32 consecutive rows fall in distinct banks.
+__host__ __device__ constexpr int64_t split_reduce_bytes(int rows, int bn, int splits) {
+  return static_cast<int64_t>(splits) * ((rows + splits - 1) / splits) * (bn + 4) * 4;
+}
 
 struct SplitShape {
   int bn;           // output features per tile (multiple of 32, <= 256)
@@ -584,15 +599,14 @@ struct SplitShape {
   int kpb;          // k-steps per split
 };
 
-// Load from a cluster peer's shared memory.  Not volatile: the staged data
-// does not change between the cluster barriers around its use, so the
-// compiler may batch these loads.
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-      : "r"(addr));
-  return v;
+// 16-byte store into a cluster peer's shared memory, counted as 16
+// transaction bytes on the peer's mbarrier (both shared::cluster addresses).
+__device__ __forceinline__ void st_async_f4(uint32_t dst, float a, float b, float c, float d,
+                                            uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(dst), "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
@@ -619,9 +633,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kSplitMaxStages;
   uint64_t* acc_full = empty + kSplitMaxStages;
   uint64_t* drain = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* recv_full = drain + 1;  // the peers' partials of this CTA's rows landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_full + 1);
   int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
   volatile int32_t* abort_v = abort_flag;
+  int64_t* row_slot = reinterpret_cast<int64_t*>(smem + kSplitSlotOffset);  // [kBM]
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -630,6 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
+    mbar_init(recv_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -650,7 +667,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k0 = static_cast<int>(rank) * sh.kpb;
   const int k1 = min(p.k_iters, k0 + sh.kpb);
   const int live = static_cast<int>(p.T - m0 < kBM ? p.T - m0 : kBM);
-  float* stage_rows = reinterpret_cast<float*>(smem);  // [kBM][kStageRowWords], after the MMAs
+  // Reduction rows, over the ring once the MMAs are done: this CTA's own
+  // rows at (row - own_lo) * rs floats, then the receive slots, `per` rows
+  // per sender (sender q's slot is q, or q - 1 past this CTA's rank).
+  const int rs = bn + 4;
+  const int per = (live + splits - 1) / splits;
+  auto own_lo = [&](int q) { return min(live, q * per); };
+  auto own_n = [&](int q) { return min(live, q * per + per) - min(live, q * per); };
+  auto slot_of = [&](int sender, int owner) { return sender < owner ? sender : sender - 1; };
+  float* stage_rows = reinterpret_cast<float*>(smem);
+  float* recv_rows = stage_rows + per * rs;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -715,98 +741,126 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!__all_sync(0xffffffffu, mbar_wait(drain, 0)) && lane == 0)
       report(p.status, B200_DEV_WAIT_TIMEOUT);
   } else {
-    // Stage this CTA's partial rows (the operand ring is idle once the
-    // accumulator is complete: every copy was consumed by an MMA before it).
-    const int qd = warp & 3;
-    const int r = qd * 32 + lane;
-    if (__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(acc_full, 0))) {
-      tc_fence_after();
-      const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < bn; c += 32) {
-        float v[32];
-        __syncwarp();
-        tmem_ld32(trow + static_cast<uint32_t>(c), v);
-        tmem_wait_ld();
-        if (r < live) {
-          float4* dst = reinterpret_cast<float4*>(stage_rows + r * kStageRowWords + c);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-      }
-    } else if (lane == 0) {
+    const int r = (warp & 3) * 32 + lane;
+    // The slots of the rows this CTA stores, read while the MMAs run.
+    if (r >= own_lo(rank) && r < own_lo(rank) + own_n(rank) && n0 + bn > p.C)
+      row_slot[r] = load_index(p.slots, (m0 + r) * p.ss, p.slots_i64);
+    if (warp == 2 && lane == 0)
+      mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>((splits - 1) * own_n(rank) * bn * 4));
+    if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(acc_full, 0)) && lane == 0) {
       report(p.status, B200_DEV_WAIT_TIMEOUT);
       *abort_v = 1;
     }
     tc_fence_before();
   }
   __syncthreads();
-  cluster_sync_all();  // every partial of the cluster is staged
+  cluster_sync_all();  // every accumulator of the cluster is complete and every ring idle
+  // The peers' abort flags (read now, checked once the partials are in).
+  int32_t flag[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    flag[q] = q < splits ? ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) : 0;
+  if (warp >= 2) {
+    // Each thread sends its TMEM row to the row's owner.  A CTA whose
+    // accumulator was abandoned sends zeros, so that every owner's byte
+    // count completes; the owner then stores nothing.
+    tc_fence_after();
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    const int owner = r < live ? r / per : -1;
+    const bool mine_ok = *abort_v == 0;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    float* local = stage_rows;
+    uint32_t remote = 0, bar = 0;
+    if (owner == static_cast<int>(rank)) {
+      local = stage_rows + (r - own_lo(owner)) * rs;
+    } else if (owner >= 0) {
+      const uint32_t o = static_cast<uint32_t>(owner);
+      remote = map_to_rank(recv_rows + (slot_of(static_cast<int>(rank), owner) * per +
+                                        (r - own_lo(owner))) * rs, o);
+      bar = map_to_rank(recv_full, o);
+    }
+#pragma unroll 1
+    for (int c = 0; c < bn; c += 32) {
+      float v[32];
+      __syncwarp();
+      if (mine_ok) {
+        tmem_ld32(trow + static_cast<uint32_t>(c), v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (owner == static_cast<int>(rank)) {
+        float4* dst = reinterpret_cast<float4*>(local + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else if (owner >= 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          st_async_f4(remote + static_cast<uint32_t>((c + 4 * i) * 4), v[4 * i], v[4 * i + 1],
+                      v[4 * i + 2], v[4 * i + 3], bar);
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();  // this CTA's own rows are staged
   {
     bool all_ok = true;
-    for (int q = 0; q < splits; ++q)
-      all_ok = all_ok && ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) == 0;
-    // This CTA's items: (token lr = rank + j * splits, 4-column group) over
-    // the tile's bn columns, flattened over all the CTA's threads.  Each
-    // thread keeps kReduceBatch items' partial loads in flight at once (the
-    // loads are independent; the staging areas do not change between the
-    // two cluster barriers).
-    const int e = threadIdx.x;
-    const int ncol4 = bn / 4;
-    const int mine = live > static_cast<int>(rank)
-                         ? (live - static_cast<int>(rank) + splits - 1) / splits : 0;
-    const int items = all_ok ? mine * ncol4 : 0;
-    constexpr int kReduceBatch = 8;
-    for (int base = e; base < items; base += kThreads * kReduceBatch) {
-      float4 acc[kReduceBatch];
-      uint32_t off[kReduceBatch];
 #pragma unroll
-      for (int u = 0; u < kReduceBatch; ++u) {
-        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int it = min(base + u * kThreads, items - 1);
-        const int lr = static_cast<int>(rank) + (it / ncol4) * splits;
-        off[u] = static_cast<uint32_t>((lr * kStageRowWords + (it % ncol4) * 4) * 4);
-      }
+    for (int q = 0; q < 8; ++q) all_ok = all_ok && flag[q] == 0;
+    const int lo = own_lo(static_cast<int>(rank));
+    const int n_own = own_n(static_cast<int>(rank));
+    bool ready = n_own > 0;
+    if (ready && !mbar_wait(recv_full, 0)) {
+      report(p.status, B200_DEV_WAIT_TIMEOUT);
+      ready = false;
+    }
+    // Items (owned row, 32-column run), rows fastest: a warp's 16-byte
+    // loads of one run cover consecutive rows.
+    const int items = ready && all_ok ? n_own * (bn / 32) : 0;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int lr = it % n_own;
+      const int c = (it / n_own) * 32;
+      const int64_t n = n0 + c;
+      if (n >= 3 * p.C) continue;
+      float acc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
       for (int q = 0; q < splits; ++q) {
-        const uint32_t peer = map_to_rank(stage_rows, static_cast<uint32_t>(q));
-        float4 v[kReduceBatch];
+        const float* src = q == static_cast<int>(rank)
+                               ? stage_rows + lr * rs + c
+                               : recv_rows + (slot_of(q, static_cast<int>(rank)) * per + lr) * rs + c;
 #pragma unroll
-        for (int u = 0; u < kReduceBatch; ++u) v[u] = ld_cluster_f4(peer + off[u]);
-#pragma unroll
-        for (int u = 0; u < kReduceBatch; ++u) {
-          acc[u].x += v[u].x;
-          acc[u].y += v[u].y;
-          acc[u].z += v[u].z;
-          acc[u].w += v[u].w;
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = reinterpret_cast<const float4*>(src)[i];
+          acc[4 * i] += v.x;
+          acc[4 * i + 1] += v.y;
+          acc[4 * i + 2] += v.z;
+          acc[4 * i + 3] += v.w;
         }
       }
-#pragma unroll
-      for (int u = 0; u < kReduceBatch; ++u) {
-        const int it = base + u * kThreads;
-        if (it >= items) continue;
-        const int lr = static_cast<int>(rank) + (it / ncol4) * splits;
-        const int64_t n = n0 + (it % ncol4) * 4;
-        if (n >= 3 * p.C) continue;
-        const int64_t row = m0 + lr;
-        const uint2 w2 = make_uint2(pack_bf16(acc[u].x, acc[u].y), pack_bf16(acc[u].z, acc[u].w));
-        if (n < p.C) {
-          *reinterpret_cast<uint2*>(p.q_out + row * p.q_rs + n) = w2;
+      const int64_t row = m0 + lo + lr;
+      // C is a multiple of 64, so a 32-column run never straddles thirds.
+      if (n < p.C) {
+        store_run32(p.q_out + row * p.q_rs + n, acc);
+      } else {
+        const int64_t slot = row_slot[lo + lr];
+        if (slot < 0 || slot >= p.nslots) {
+          report(p.status, B200_DEV_BAD_SLOT);
+        } else if (n < 2 * p.C) {
+          store_run32(p.k_pool + (p.row0 + slot) * p.C + (n - p.C), acc);
         } else {
-          const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
-          if (slot < 0 || slot >= p.nslots) {
-            report(p.status, B200_DEV_BAD_SLOT);
-          } else if (n < 2 * p.C) {
-            *reinterpret_cast<uint2*>(p.k_pool + (p.row0 + slot) * p.C + (n - p.C)) = w2;
-          } else {
-            *reinterpret_cast<uint2*>(p.v_pool + (p.row0 + slot) * p.C + (n - 2 * p.C)) = w2;
-          }
+          store_run32(p.v_pool + (p.row0 + slot) * p.C + (n - 2 * p.C), acc);
         }
       }
     }
   }
   __syncthreads();
-  cluster_sync_all();  // no CTA leaves while a peer may still read its staging area
+  // No CTA leaves while a store into its shared memory may be in flight:
+  // every owner has seen its partials land before this barrier.
+  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -992,13 +1046,16 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
   // still end inside the ring.
   auto ring_stages = [&](int kc) {
     const int sb = kc * (sh.xrows + sh.bn) * 128;
-    return std::min({kSplitMaxStages, kRingBytes / sb,
-                     (kRingBytes - kBM * 128 - (kc - 1) * sh.xrows * 128) / sb + 1});
+    return std::min({kSplitMaxStages, kSplitAreaBytes / sb,
+                     (kSplitAreaBytes - kBM * 128 - (kc - 1) * sh.xrows * 128) / sb + 1});
   };
   sh.kc = ring_stages(2) >= 3 ? 2 : 1;
   sh.stage_bytes = sh.kc * (sh.xrows + sh.bn) * 128;
   sh.stages = ring_stages(sh.kc);
   sh.splits = plan.splits;
+  if (sh.splits < 1 || sh.splits > 8 ||
+      split_reduce_bytes(sh.xrows, sh.bn, sh.splits) > kSplitAreaBytes)
+    return fail(B200_ERR_UNSUPPORTED, "qkv projection: split plan exceeds the reduction area");
   CUtensorMap tx, tw;
   {
     // {64 columns, token rows, 64-column chunks}: the chunk dimension
@@ -1048,11 +1105,12 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
 QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
-  if (m_tiles <= 2 && T > 64) {
-    // 65..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
+  if (m_tiles <= 2 && T > 96) {
+    // 97..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
     // 256) beats split-K clusters once those tiles fit in one wave: at
-    // hidden 4096, 128 tokens take 25.0 us on single CTAs against 29.3 us
-    // split-K, and 256 tokens 31.0 us on CTA pairs against 47.0 us.
+    // hidden 4096, 128 tokens take 23.2 us on single CTAs against 23.5 us
+    // split-K, and 256 tokens 29.3 us on CTA pairs against 33.6 us (96
+    // tokens: 21.9 us split-K, 22.6 us single CTAs).
     const int64_t single_tiles = ceil_div(3 * C, 128);
     const int64_t pair_tiles = ceil_div(3 * C, kPairBN);
     if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
@@ -1071,6 +1129,7 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
       const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
       for (int s = 1; s <= 8; ++s) {
         if (tiles * s > num_sms || (s > 1 && k_iters / s < 8)) continue;
+        if (split_reduce_bytes(xrows, bn, s) > kSplitAreaBytes) continue;
         if (s > 1 && tiles > split_capacity(s, dev)) continue;
         const int64_t cost = ceil_div(k_iters, s) * (xrows + bn);
         if (best_cost < 0 || cost < best_cost) {
