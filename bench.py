@@ -114,9 +114,10 @@ class DecodeWorkload:
                          f" requests {per} x {lens[0]} tokens, H=32, D=128, S=16, fused KV write")
         else:
             self.global_B = batch or 256
-            # Configuration 3: contexts ~U[1, 4096] (seed 0), the first one 1
-            # and the last one forced to a non-multiple of the block size.
-            g = torch.Generator().manual_seed(0 if strong else rank)
+            # Configuration 3: contexts ~U[1, 4096] (seed 0 on every rank, so
+            # each rank of the weak-scaling run has the same work), the first
+            # one 1 and the last one forced to a non-multiple of the block size.
+            g = torch.Generator().manual_seed(0)
             lens = torch.randint(1, 4097, (self.global_B,), generator=g).tolist()
             lens[0] = 1
             if lens[-1] % S == 0:
@@ -206,8 +207,11 @@ class PrefillWorkload:
     def __init__(self, T, rank, device, nseq=16):
         self.T, self.device, self.nseq = T, device, nseq
         self.bound = "tensor" if T >= 512 else "hbm"
+        # The prefixes come from seed 0 on every rank (each rank of the
+        # weak-scaling run has the same work); the tensors' values from the rank.
+        self.prefix = (torch.randint(0, 253, (nseq,), generator=torch.Generator().manual_seed(0))
+                       * 16).tolist()
         g = torch.Generator().manual_seed(rank)
-        self.prefix = (torch.randint(0, 253, (nseq,), generator=g) * 16).tolist()
         counts = [math.ceil((p + T) / S) for p in self.prefix]
         P = sum(counts) + 16
         gd = torch.Generator(device=device).manual_seed(30260000 + rank)

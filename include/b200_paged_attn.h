@@ -267,8 +267,8 @@ B200_API int b200_qkv_kv_write(const b200_qkv_kv_write_args_t* args, void* strea
 
 /* The kernel b200_qkv_kv_write launches for num_tokens x hidden on the
  * current device: *kind = 0 single CTAs (128 x *tile_n tiles), 1 CTA pairs
- * (256 x 256 tiles), 2 split-K clusters of *splits CTAs (128 x *tile_n
- * tiles).  A diagnostic with no counterpart in the reference. */
+ * (256 x *tile_n tiles, *tile_n 192 or 256), 2 split-K clusters of *splits
+ * CTAs (128 x *tile_n tiles).  A diagnostic with no counterpart in the reference. */
 B200_API int b200_qkv_kv_write_plan(int64_t num_tokens, int64_t hidden, int32_t* kind,
                                     int32_t* tile_n, int32_t* splits);
 

@@ -16,7 +16,8 @@
 // into the row's slot and k and v never exist as a separate tensor.
 //
 // Three kernels share the warp roles below; qkv_plan picks one per call:
-//   CTA pairs   long token runs: 256 x 256 tiles, tcgen05.mma.cta_group::2;
+//   CTA pairs   129+ tokens: 256 x BN tiles, tcgen05.mma.cta_group::2 (BN =
+//               192 up to 256 tokens, where it keeps more SMs busy, else 256);
 //   single CTA  128 x BN tiles (BN = 64 or 128) where those waves are
 //               cheaper than pair waves;
 //   split-K     decode-size token counts (<= 256): one output tile per
@@ -312,11 +313,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ CTA pairs
-// For long token runs the tiles are 256 tokens x 256 features, computed by
+// For long token runs the tiles are 256 tokens x BN features, computed by
 // a cluster of two CTAs with tcgen05.mma.cta_group::2: CTA r of the pair
-// loads token rows [128r, +128) of the x tile and feature rows [128r, +128)
-// of the W tile, and the pair MMA (issued by CTA 0 only) multiplies the
-// pair's 256 x rows by all 256 W rows, each CTA's TMEM receiving the
+// loads token rows [128r, +128) of the x tile and feature rows
+// [BN/2 * r, +BN/2) of the W tile, and the pair MMA (issued by CTA 0 only)
+// multiplies the pair's 256 x rows by all BN W rows, each CTA's TMEM receiving the
 // accumulator rows of its own tokens.  Per SM this halves the W bytes
 // staged in shared memory for the same tensor work, which a single CTA
 // with 256-wide tiles is limited by.  Both CTAs' copies complete on CTA 0's
@@ -324,24 +325,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 // publish each accumulator to both epilogues; each epilogue warp of either
 // CTA returns an accumulator to CTA 0 with one remote arrival.  Each CTA
 // loads only its own rows: every TMA copy writes the issuing CTA's shared
-// memory alone.
+// memory alone.  BN is 256 for long token runs (the fewest staged bytes
+// per MAC) or 192 for 129-256 tokens (3C / 192 pairs keep more SMs busy).
 constexpr int kPairBN = 256;
+constexpr int kPairBNNarrow = 192;
+template <int BN>
 struct PairCfg {
   static constexpr int A_BYTES = kBM * 128;        // this CTA's 128 x rows
-  static constexpr int B_BYTES = 128 * 128;        // this CTA's 128 W rows
+  static constexpr int B_BYTES = (BN / 2) * 128;   // this CTA's BN/2 W rows
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = kRingBytes / STAGE;  // 6
   static constexpr int BAR = STAGES * STAGE;
   static constexpr int BYTES = BAR + 256;
-  static constexpr int TMEM_COLS = 2 * kPairBN;    // two 256-column accumulators
+  static constexpr int TMEM_COLS = 512;            // two BN-column accumulators (a power of 2)
+  static_assert(2 * BN <= TMEM_COLS, "two accumulators must fit the allocation");
   static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
   static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area too small");
 };
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     qkv_kv_write_pair_kernel(const __grid_constant__ CUtensorMap tmx,
                              const __grid_constant__ CUtensorMap tmw, const QkvParams p) {
-  using Cfg = PairCfg;
+  using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -401,7 +407,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int mt, nt;
         tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
         const int m0 = mt * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = nt * kPairBN + static_cast<int>(rank) * 128;
+        const int n0 = nt * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < p.k_iters; ++kb) {
           const int st = static_cast<int>(issued % STAGES);
           const uint32_t use = static_cast<uint32_t>(issued / STAGES);
@@ -436,7 +442,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
         return __all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(bar, parity)) != 0;
       };
-      constexpr uint32_t idesc = idesc_bf16(2 * kBM, kPairBN, false);
+      constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN, false);
       const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
       int64_t consumed = 0;
       bool ok = true;
@@ -449,7 +455,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t td = tmem + static_cast<uint32_t>(acc * kPairBN);
+        const uint32_t td = tmem + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < p.k_iters; ++kb, ++consumed) {
           const int st = static_cast<int>(consumed % STAGES);
           if (!wait_all(&full[st], static_cast<uint32_t>(consumed / STAGES) & 1u)) {
@@ -496,10 +502,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int mt, nt;
       tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
       const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + qd * 32 + lane;
-      const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
+      const int64_t n0 = static_cast<int64_t>(nt) * BN;
       const bool live = row < p.T;
       int64_t dst_row = -1;
-      if (live && n0 + kPairBN > p.C) {
+      if (live && n0 + BN > p.C) {
         const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
         if (slot >= 0 && slot < p.nslots) {
           dst_row = (p.row0 + slot) * p.C;
@@ -507,9 +513,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           report(p.status, B200_DEV_BAD_SLOT);
         }
       }
-      const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * kPairBN);
+      const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < kPairBN; c += 32) {
+      for (int c = 0; c < BN; c += 32) {
         float v[32];
         __syncwarp();
         tmem_ld32(tacc + static_cast<uint32_t>(c), v);
@@ -946,22 +952,23 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
   return B200_OK;
 }
 
+template <int BN>
 int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const DeviceInfo& dev) {
-  using Cfg = PairCfg;
+  using Cfg = PairCfg<BN>;
   const int64_t T = a.num_tokens, C = a.hidden;
   const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
   if (smem > static_cast<size_t>(dev.max_smem_optin))
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
   CUtensorMap tx, tw;
   int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
-  if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, 128);  // this CTA's half
+  if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, BN / 2);  // this CTA's half
   if (rc != B200_OK) return rc;
   static std::atomic<int> max_pairs[64];
   int pairs = dev.num_sms / 2;
   if (dev.device >= 0 && dev.device < 64) {
     if (max_pairs[dev.device].load(std::memory_order_acquire) == 0) {
       std::lock_guard<std::mutex> lock(g_setup_mu);
-      cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_pair_kernel,
+      cudaError_t e = cudaFuncSetAttribute(qkv_kv_write_pair_kernel<BN>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write_pair)");
@@ -970,7 +977,7 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
       cfg.blockDim = dim3(kThreads, 1, 1);
       cfg.dynamicSmemBytes = smem;
       int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_pair_kernel, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, qkv_kv_write_pair_kernel<BN>, &cfg);
       if (e != cudaSuccess || n < 1) {
         (void)cudaGetLastError();
         n = dev.num_sms / 2;
@@ -979,10 +986,10 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
     }
     pairs = max_pairs[dev.device].load(std::memory_order_acquire);
   }
-  const QkvParams prm = make_params(a, 2 * kBM, kPairBN, kBK);
+  const QkvParams prm = make_params(a, 2 * kBM, BN, kBK);
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, pairs));
-  qkv_kv_write_pair_kernel<<<grid, kThreads, smem, stream>>>(tx, tw, prm);
+  qkv_kv_write_pair_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "qkv_kv_write_pair launch");
   return B200_OK;
@@ -1107,14 +1114,17 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int64_t m_tiles = ceil_div(T, kBM);
   if (m_tiles <= 2 && T > 96) {
     // 97..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
-    // 256) beats split-K clusters once those tiles fit in one wave: at
+    // BN) beats split-K clusters once those tiles fit in one wave: at
     // hidden 4096, 128 tokens take 23.2 us on single CTAs against 23.5 us
     // split-K, and 256 tokens 29.3 us on CTA pairs against 33.6 us (96
-    // tokens: 21.9 us split-K, 22.6 us single CTAs).
+    // tokens: 21.9 us split-K, 22.6 us single CTAs).  Pairs take 192-wide
+    // tiles when those fit one wave too: more SMs, fewer bytes each.
     const int64_t single_tiles = ceil_div(3 * C, 128);
-    const int64_t pair_tiles = ceil_div(3 * C, kPairBN);
     if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
-    if (m_tiles == 2 && pair_tiles <= num_sms / 2) return {QkvPlan::kPair, kPairBN, 1, kBM};
+    if (m_tiles == 2 && ceil_div(3 * C, kPairBNNarrow) <= num_sms / 2)
+      return {QkvPlan::kPair, kPairBNNarrow, 1, kBM};
+    if (m_tiles == 2 && ceil_div(3 * C, kPairBN) <= num_sms / 2)
+      return {QkvPlan::kPair, kPairBN, 1, kBM};
   }
   if (m_tiles <= 2) {
     // Few tokens (decode): the weights dominate and are read once, at a
@@ -1167,7 +1177,9 @@ int launch_qkv_kv_write(const b200_qkv_kv_write_args_t& a, cudaStream_t stream) 
   int rc = current_device_info(&dev);
   if (rc != B200_OK) return rc;
   const QkvPlan plan = qkv_plan(a.num_tokens, a.hidden, dev);
-  if (plan.kind == QkvPlan::kPair) return launch_pair(a, stream, dev);
+  if (plan.kind == QkvPlan::kPair)
+    return plan.bn == kPairBNNarrow ? launch_pair<kPairBNNarrow>(a, stream, dev)
+                                    : launch_pair<kPairBN>(a, stream, dev);
   if (plan.kind == QkvPlan::kSplit) return launch_split(a, stream, plan, dev);
   switch (plan.bn) {
     case 128:
