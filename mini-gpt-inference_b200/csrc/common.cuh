@@ -158,11 +158,6 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Named barrier over `count` threads (multiple of 32).
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
 // Packed fp32x2 fused multiply-add (one sm_100 instruction for two lanes of
