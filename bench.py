@@ -392,16 +392,46 @@ class QkvWorkload:
     def extra(self, value, ms_max, world, steps):
         """The unfused sequence the kernel replaces, timed the same way:
         torch's bf16 matmul (cuBLAS) into a [T, 3C] tensor, then the
-        slot-mapping scatter of its k and v thirds."""
+        slot-mapping scatter of its k and v thirds (a prepared call).  The
+        ``cuda_graph`` entry times the fused call and both unfused sequences
+        as CUDA graphs of 10 calls, device time without host overhead, which
+        at decode sizes is larger than the kernels themselves."""
         from b200attn import kv_scatter_b200
         T, C = self.T, self.C
-        y = torch.empty((T, 3 * C), dtype=torch.bfloat16, device=self.device)
+        dev = self.device
+        y = torch.empty((T, 3 * C), dtype=torch.bfloat16, device=dev)
+        with torch.inference_mode():
+            scatter_call = kv_scatter_b200(y[:, C:2 * C].view(T, H, D), y[:, 2 * C:].view(T, H, D),
+                                           self.pool, self.slots, 0, prepare=True)
 
         def unfused(scatter):
             torch.matmul(self.x, self.w.t(), out=y)
             if scatter:
-                kv_scatter_b200(y[:, C:2 * C].view(T, H, D), y[:, 2 * C:].view(T, H, D),
-                                self.pool, self.slots, 0)
+                scatter_call()
+
+        def graph_ms(fn, calls=10, reps=20):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(calls):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / (reps * calls)
+            del graph
+            return ms
 
         res = {}
         with torch.inference_mode():
@@ -413,12 +443,15 @@ class QkvWorkload:
                 for _ in range(steps):
                     unfused(scatter)
                 e1.record()
-                torch.cuda.synchronize(self.device)
+                torch.cuda.synchronize(dev)
                 ms = e0.elapsed_time(e1) / steps
                 key = "cublas_matmul_plus_scatter" if scatter else "cublas_matmul_alone"
                 res[key] = {"ms_per_step": ms,
                             "value": self.work() / (ms * 1e-3) / (1e12 if self.bound == "tensor" else 1e9),
                             "unit": self.unit}
+            res["cuda_graph"] = {"fused_ms_per_call": graph_ms(self.call),
+                                 "cublas_matmul_alone_ms_per_call": graph_ms(lambda: unfused(False)),
+                                 "cublas_matmul_plus_scatter_ms_per_call": graph_ms(lambda: unfused(True))}
         res["fused_ms_per_step"] = ms_max / steps
         return {"unfused_comparison": res}
 
