@@ -673,6 +673,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k0 = static_cast<int>(rank) * sh.kpb;
   const int k1 = min(p.k_iters, k0 + sh.kpb);
   const int live = static_cast<int>(p.T - m0 < kBM ? p.T - m0 : kBM);
+  // Up to 64 token rows the MMAs are M = 64: they read half the A rows.  The
+  // M = 64 accumulator puts rows 16q .. 16q + 15 in TMEM lanes 32q .. 32q + 15;
+  // acc_row gives the row that lane `lane` of lane quarter q holds (-1: none).
+  const int mma_m = sh.xrows <= 64 ? 64 : kBM;
+  auto acc_row = [&](int q, int ln) { return mma_m == 64 ? (ln < 16 ? q * 16 + ln : -1) : q * 32 + ln; };
   // Reduction rows, over the ring once the MMAs are done: this CTA's own
   // rows at (row - own_lo) * rs floats, then the receive slots, `per` rows
   // per sender (sender q's slot is q, or q - 1 past this CTA's rank).
@@ -714,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
   } else if (warp == 1) {
-    const uint32_t idesc = idesc_bf16(kBM, bn, false);
+    const uint32_t idesc = idesc_bf16(mma_m, bn, false);
     const uint64_t da0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
     bool ok = true;
     for (int kb = k0, j = 0; kb < k1; ++kb, ++j) {
@@ -747,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!__all_sync(0xffffffffu, mbar_wait(drain, 0)) && lane == 0)
       report(p.status, B200_DEV_WAIT_TIMEOUT);
   } else {
-    const int r = (warp & 3) * 32 + lane;
+    const int r = acc_row(warp & 3, lane);
     // The slots of the rows this CTA stores, read while the MMAs run.
     if (r >= own_lo(rank) && r < own_lo(rank) + own_n(rank) && n0 + bn > p.C)
       row_slot[r] = load_index(p.slots, (m0 + r) * p.ss, p.slots_i64);
@@ -772,8 +777,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // count completes; the owner then stores nothing.
     tc_fence_after();
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;
-    const int owner = r < live ? r / per : -1;
+    const int r = acc_row(qd, lane);
+    const int owner = r >= 0 && r < live ? r / per : -1;
     const bool mine_ok = *abort_v == 0;
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     float* local = stage_rows;
