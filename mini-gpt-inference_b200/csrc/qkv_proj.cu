@@ -43,6 +43,7 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -101,14 +102,16 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   nt = r / rows;
 }
 
-// Stores 32 f32 values as 32 bf16 (64 contiguous bytes, 16-byte aligned).
-__device__ __forceinline__ void store_run32(__nv_bfloat16* dst, const float* v) {
+// Stores RW f32 values as RW bf16 (2 * RW contiguous bytes, 16-byte aligned).
+template <int RW>
+__device__ __forceinline__ void store_run(__nv_bfloat16* dst, const float* v) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < RW / 8; ++i)
     d[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
                       pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
 }
+__device__ __forceinline__ void store_run32(__nv_bfloat16* dst, const float* v) { store_run<32>(dst, v); }
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -556,7 +559,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // at most ~90 GB/s into one SM, so the weight stream must be spread over
 // nearly every SM with as few bytes per SM as possible.  One tile per CTA
 // of 256 features would use only 3C / 256 SMs (48 at C = 4096); instead
-// the tile width (a multiple of 32, <= 256) and a split of the reduction
+// the tile width (a multiple of 16, <= 256) and a split of the reduction
 // over a cluster of `splits` CTAs are chosen per call: CTA r of a cluster
 // accumulates k-steps [r * kpb, +kpb) of one output tile in its own TMEM.
 // The x box is only as tall as the live tokens (rows of the A operand past
@@ -596,7 +599,7 @@ __host__ __device__ constexpr int64_t split_reduce_bytes(int rows, int bn, int s
 }
 
 struct SplitShape {
-  int bn;           // output features per tile (multiple of 32, <= 256)
+  int bn;           // output features per tile (multiple of 16, <= 256)
   int xrows;        // x box rows (multiple of 8, <= 128)
   int kc;           // 64-column chunks per stage (1 or 2)
   int stage_bytes;  // kc * (xrows + bn) * 128
@@ -802,16 +805,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
+      // Only the tile's bn columns are sent (bn may end half-way into a
+      // 32-column load).
       if (owner == static_cast<int>(rank)) {
         float4* dst = reinterpret_cast<float4*>(local + c);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          if (c + 4 * i < bn) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       } else if (owner >= 0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_async_f4(remote + static_cast<uint32_t>((c + 4 * i) * 4), v[4 * i], v[4 * i + 1],
-                      v[4 * i + 2], v[4 * i + 3], bar);
+          if (c + 4 * i < bn)
+            st_async_f4(remote + static_cast<uint32_t>((c + 4 * i) * 4), v[4 * i], v[4 * i + 1],
+                        v[4 * i + 2], v[4 * i + 3], bar);
       }
     }
     tc_fence_before();
@@ -828,45 +834,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       report(p.status, B200_DEV_WAIT_TIMEOUT);
       ready = false;
     }
-    // Items (owned row, 32-column run), rows fastest: a warp's 16-byte
-    // loads of one run cover consecutive rows.
-    const int items = ready && all_ok ? n_own * (bn / 32) : 0;
-    for (int it = threadIdx.x; it < items; it += kThreads) {
-      const int lr = it % n_own;
-      const int c = (it / n_own) * 32;
-      const int64_t n = n0 + c;
-      if (n >= 3 * p.C) continue;
-      float acc[32];
+    // Items (owned row, RW-column run), rows fastest: a warp's 16-byte
+    // loads of one run cover consecutive rows.  Runs are 32 columns, or 16
+    // when bn is not a multiple of 32 (a 32-column run could then straddle
+    // the q / k / v boundaries, which are multiples of 64).
+    auto sum_pass = [&](auto run_width) {
+      constexpr int RW = decltype(run_width)::value;
+      const int items = ready && all_ok ? n_own * (bn / RW) : 0;
+      for (int it = threadIdx.x; it < items; it += kThreads) {
+        const int lr = it % n_own;
+        const int c = (it / n_own) * RW;
+        const int64_t n = n0 + c;
+        if (n >= 3 * p.C) continue;
+        float acc[RW];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-      for (int q = 0; q < splits; ++q) {
-        const float* src = q == static_cast<int>(rank)
-                               ? stage_rows + lr * rs + c
-                               : recv_rows + (slot_of(q, static_cast<int>(rank)) * per + lr) * rs + c;
+        for (int i = 0; i < RW; ++i) acc[i] = 0.f;
+        for (int q = 0; q < splits; ++q) {
+          const float* src = q == static_cast<int>(rank)
+                                 ? stage_rows + lr * rs + c
+                                 : recv_rows + (slot_of(q, static_cast<int>(rank)) * per + lr) * rs + c;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 v = reinterpret_cast<const float4*>(src)[i];
-          acc[4 * i] += v.x;
-          acc[4 * i + 1] += v.y;
-          acc[4 * i + 2] += v.z;
-          acc[4 * i + 3] += v.w;
+          for (int i = 0; i < RW / 4; ++i) {
+            const float4 v = reinterpret_cast<const float4*>(src)[i];
+            acc[4 * i] += v.x;
+            acc[4 * i + 1] += v.y;
+            acc[4 * i + 2] += v.z;
+            acc[4 * i + 3] += v.w;
+          }
         }
-      }
-      const int64_t row = m0 + lo + lr;
-      // C is a multiple of 64, so a 32-column run never straddles thirds.
-      if (n < p.C) {
-        store_run32(p.q_out + row * p.q_rs + n, acc);
-      } else {
-        const int64_t slot = row_slot[lo + lr];
-        if (slot < 0 || slot >= p.nslots) {
-          report(p.status, B200_DEV_BAD_SLOT);
-        } else if (n < 2 * p.C) {
-          store_run32(p.k_pool + (p.row0 + slot) * p.C + (n - p.C), acc);
+        const int64_t row = m0 + lo + lr;
+        if (n < p.C) {
+          store_run<RW>(p.q_out + row * p.q_rs + n, acc);
         } else {
-          store_run32(p.v_pool + (p.row0 + slot) * p.C + (n - 2 * p.C), acc);
+          const int64_t slot = row_slot[lo + lr];
+          if (slot < 0 || slot >= p.nslots) {
+            report(p.status, B200_DEV_BAD_SLOT);
+          } else if (n < 2 * p.C) {
+            store_run<RW>(p.k_pool + (p.row0 + slot) * p.C + (n - p.C), acc);
+          } else {
+            store_run<RW>(p.v_pool + (p.row0 + slot) * p.C + (n - 2 * p.C), acc);
+          }
         }
       }
-    }
+    };
+    if (bn % 32 == 0)
+      sum_pass(std::integral_constant<int, 32>{});
+    else
+      sum_pass(std::integral_constant<int, 16>{});
   }
   __syncthreads();
   // No CTA leaves while a store into its shared memory may be in flight:
@@ -1140,7 +1154,7 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
     const int xrows = m_tiles == 1 ? static_cast<int>((T + 7) / 8 * 8) : kBM;
     QkvPlan best{QkvPlan::kSplit, 0, 0, 0};
     int64_t best_cost = -1;
-    for (int bn = kSplitMaxBN; bn >= 32; bn -= 32) {
+    for (int bn = kSplitMaxBN; bn >= 32; bn -= 16) {
       const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
       for (int s = 1; s <= 8; ++s) {
         if (tiles * s > num_sms || (s > 1 && k_iters / s < 8)) continue;

@@ -254,7 +254,7 @@ def test_qkv_plan_covers_each_kernel(T, C, kind):
     assert lib.b200_qkv_kv_write_plan(T, C, ctypes.byref(k), ctypes.byref(n), ctypes.byref(s)) == 0
     assert k.value == kind, (k.value, n.value, s.value)
     if kind == 2:
-        assert 1 <= s.value <= 8 and n.value % 32 == 0
+        assert 1 <= s.value <= 8 and n.value % 16 == 0
     if kind == 1:
         # 192-wide pair tiles for 129-256 tokens (more SMs), 256-wide for long runs.
         assert n.value == (192 if T <= 256 else 256), n.value
