@@ -1131,13 +1131,13 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
 QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
-  if (m_tiles <= 2 && T > 96) {
-    // 97..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
+  if (m_tiles <= 2 && T > 120) {
+    // 121..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
     // BN) beats split-K clusters once those tiles fit in one wave: at
-    // hidden 4096, 128 tokens take 23.2 us on single CTAs against 23.5 us
-    // split-K, and 256 tokens 29.3 us on CTA pairs against 33.6 us (96
-    // tokens: 21.9 us split-K, 22.6 us single CTAs).  Pairs take 192-wide
-    // tiles when those fit one wave too: more SMs, fewer bytes each.
+    // hidden 4096, 128 tokens take 23.0 us on single CTAs against 23.6 us
+    // split-K, and 256 tokens 26.9 us on 192-wide CTA pairs against 33.6 us
+    // (112 tokens: 21.7 us split-K, 22.6 us single CTAs).  Pairs take
+    // 192-wide tiles when those fit one wave too: more SMs, fewer bytes each.
     const int64_t single_tiles = ceil_div(3 * C, 128);
     if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
     if (m_tiles == 2 && ceil_div(3 * C, kPairBNNarrow) <= num_sms / 2)

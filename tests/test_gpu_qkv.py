@@ -76,7 +76,7 @@ def _check_pool(c, y, status_bits=0):
     (96, 4096, 32, 16, 1, 0),    # split-K clusters, 48 rows owned per cluster rank
     (77, 4096, 32, 16, 1, 0),    # split-K clusters, ragged owned rows (39 + 38)
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
-    (100, 1024, 8, 16, 1, 0),    # single CTAs, 128-wide tiles, 16 k-steps
+    (100, 1024, 8, 16, 1, 0),    # split-K clusters at hidden 1024 (16 k-steps)
     (129, 4096, 32, 16, 2, 1),   # CTA pairs (192-wide tiles); the second CTA holds one token
     (128, 4096, 32, 16, 1, 0),   # single CTAs, 128-wide tiles, one wave
     (256, 4096, 32, 16, 1, 0),   # CTA pairs, 192-wide tiles, one wave
@@ -238,7 +238,7 @@ def test_qkv_kv_write_full_size_against_cublas():
 
 
 @pytest.mark.parametrize("T,C,kind", [
-    (1, 4096, 2), (64, 4096, 2), (96, 4096, 2), (100, 1024, 0), (128, 4096, 0), (129, 4096, 1),
+    (1, 4096, 2), (64, 4096, 2), (96, 4096, 2), (120, 4096, 2), (100, 1024, 2), (128, 4096, 0), (129, 4096, 1),
     (256, 4096, 1), (200, 6400, 0), (300, 512, 0), (384, 4096, 0), (512, 4096, 1),
     (1000, 4096, 1), (8192, 4096, 1),
 ])
