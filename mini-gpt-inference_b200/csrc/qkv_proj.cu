@@ -570,10 +570,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // each thread reads its TMEM row and writes it to the row's owner: into
 // its own staging rows, or with st.async into the owner's receive slot for
 // this CTA, completing as transaction bytes on the owner's recv_full
-// barrier.  The owner then sums its rows' partials in rank order (the same
-// order every run) from its own shared memory, rounds once to bf16 and
-// stores 32-column runs; the (row, run) items are spread over all of the
-// CTA's threads.  The slot of each owned row is read while the MMAs run.
+// barrier; each sender's abort flag travels the same way.  The owner then
+// sums its rows' partials in rank order (the same order every run) from
+// its own shared memory, rounds once to bf16 and stores 32- (or 16-)
+// column runs; the (row, run) items are spread over all of the CTA's
+// threads.  The slot of each owned row is read while the MMAs run.  After
+// the one cluster barrier no CTA reads another's shared memory, and every
+// CTA written to waits for its bytes, so no barrier is needed at the end.
 constexpr int kSplitMaxBN = 256;
 // A stage holds kc (1 or 2) consecutive 64-column chunks of x and W,
 // fetched by one 3-D box per operand ({64 columns, rows, chunks}; the chunk
@@ -588,7 +591,8 @@ constexpr int kSplitAreaBytes = 224 * 1024;
 constexpr int kSplitBarOffset = kSplitAreaBytes;
 constexpr int kSplitSlotOffset = kSplitBarOffset + 512;
 constexpr int kSplitBytes = kSplitSlotOffset + kBM * 8;
-static_assert((2 * kSplitMaxStages + 3) * 8 + 8 <= 512, "barrier area too small");
+constexpr int kSplitMaxCluster = 8;  // splits per cluster
+static_assert((2 * kSplitMaxStages + 3) * 8 + 8 + 4 * kSplitMaxCluster <= 512, "barrier area too small");
 
 // Bytes of the reduction area for `rows` live token rows: this CTA's own
 // rows, then a receive slot per peer, ceil(rows / splits) rows each.  Rows
@@ -618,10 +622,11 @@ __device__ __forceinline__ void st_async_f4(uint32_t dst, float a, float b, floa
       : "memory");
 }
 
-__device__ __forceinline__ int32_t ld_cluster_s32(uint32_t addr) {
-  int32_t v;
-  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-  return v;
+// 4-byte form of st_async_f4.
+__device__ __forceinline__ void st_async_b32(uint32_t dst, int32_t v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+               ::"r"(dst), "r"(v), "r"(bar)
+               : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -645,6 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* recv_full = drain + 1;  // the peers' partials of this CTA's rows landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_full + 1);
   int32_t* abort_flag = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  // The abort flag of each sender of this CTA's rows (slot order), pushed
+  // with the rows.
+  int32_t* peer_flag = abort_flag + 1;  // [kSplitMaxCluster - 1]
   volatile int32_t* abort_v = abort_flag;
   int64_t* row_slot = reinterpret_cast<int64_t*>(smem + kSplitSlotOffset);  // [kBM]
 
@@ -760,7 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (r >= own_lo(rank) && r < own_lo(rank) + own_n(rank) && n0 + bn > p.C)
       row_slot[r] = load_index(p.slots, (m0 + r) * p.ss, p.slots_i64);
     if (warp == 2 && lane == 0)
-      mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>((splits - 1) * own_n(rank) * bn * 4));
+      mbar_arrive_expect_tx(recv_full, static_cast<uint32_t>(
+                                           own_n(rank) > 0 ? (splits - 1) * (own_n(rank) * bn * 4 + 4) : 0));
     if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(acc_full, 0)) && lane == 0) {
       report(p.status, B200_DEV_WAIT_TIMEOUT);
       *abort_v = 1;
@@ -769,20 +778,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   cluster_sync_all();  // every accumulator of the cluster is complete and every ring idle
-  // The peers' abort flags (read now, checked once the partials are in).
-  int32_t flag[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    flag[q] = q < splits ? ld_cluster_s32(map_to_rank(abort_flag, static_cast<uint32_t>(q))) : 0;
   if (warp >= 2) {
-    // Each thread sends its TMEM row to the row's owner.  A CTA whose
+    // Each thread sends its TMEM row to the row's owner; the thread holding
+    // an owner's first row also sends this CTA's abort flag.  A CTA whose
     // accumulator was abandoned sends zeros, so that every owner's byte
-    // count completes; the owner then stores nothing.
+    // count completes; its flag tells the owner to store nothing.  No CTA
+    // reads another's shared memory, so none need wait for the others at
+    // the end: an owner leaves only once its bytes have landed.
     tc_fence_after();
     const int qd = warp & 3;
     const int r = acc_row(qd, lane);
     const int owner = r >= 0 && r < live ? r / per : -1;
-    const bool mine_ok = *abort_v == 0;
+    const int32_t my_flag = *abort_v;
+    const bool mine_ok = my_flag == 0;
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     float* local = stage_rows;
     uint32_t remote = 0, bar = 0;
@@ -790,43 +798,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       local = stage_rows + (r - own_lo(owner)) * rs;
     } else if (owner >= 0) {
       const uint32_t o = static_cast<uint32_t>(owner);
-      remote = map_to_rank(recv_rows + (slot_of(static_cast<int>(rank), owner) * per +
-                                        (r - own_lo(owner))) * rs, o);
+      const int slot = slot_of(static_cast<int>(rank), owner);
+      remote = map_to_rank(recv_rows + (slot * per + (r - own_lo(owner))) * rs, o);
       bar = map_to_rank(recv_full, o);
+      if (r == own_lo(owner)) st_async_b32(map_to_rank(peer_flag + slot, o), my_flag, bar);
     }
-#pragma unroll 1
-    for (int c = 0; c < bn; c += 32) {
-      float v[32];
-      __syncwarp();
+    // The next 32 columns load from TMEM while the current ones are sent.
+    float v[2][32];
+    if (mine_ok) tmem_ld32(trow, v[0]);
+#pragma unroll
+    for (int i = 0; i < kSplitMaxBN / 32; ++i) {
+      const int c = i * 32;
+      if (c >= bn) break;
+      float* cur = v[i & 1];
       if (mine_ok) {
-        tmem_ld32(trow + static_cast<uint32_t>(c), v);
         tmem_wait_ld();
+        if (c + 32 < bn) tmem_ld32(trow + static_cast<uint32_t>(c + 32), v[(i + 1) & 1]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int e = 0; e < 32; ++e) cur[e] = 0.f;
       }
       // Only the tile's bn columns are sent (bn may end half-way into a
       // 32-column load).
       if (owner == static_cast<int>(rank)) {
         float4* dst = reinterpret_cast<float4*>(local + c);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (c + 4 * i < bn) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        for (int e = 0; e < 8; ++e)
+          if (c + 4 * e < bn)
+            dst[e] = make_float4(cur[4 * e], cur[4 * e + 1], cur[4 * e + 2], cur[4 * e + 3]);
       } else if (owner >= 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (c + 4 * i < bn)
-            st_async_f4(remote + static_cast<uint32_t>((c + 4 * i) * 4), v[4 * i], v[4 * i + 1],
-                        v[4 * i + 2], v[4 * i + 3], bar);
+        for (int e = 0; e < 8; ++e)
+          if (c + 4 * e < bn)
+            st_async_f4(remote + static_cast<uint32_t>((c + 4 * e) * 4), cur[4 * e], cur[4 * e + 1],
+                        cur[4 * e + 2], cur[4 * e + 3], bar);
       }
     }
     tc_fence_before();
   }
   __syncthreads();  // this CTA's own rows are staged
   {
-    bool all_ok = true;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) all_ok = all_ok && flag[q] == 0;
     const int lo = own_lo(static_cast<int>(rank));
     const int n_own = own_n(static_cast<int>(rank));
     bool ready = n_own > 0;
@@ -834,6 +845,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       report(p.status, B200_DEV_WAIT_TIMEOUT);
       ready = false;
     }
+    bool all_ok = *abort_v == 0;
+    for (int q = 0; q < splits - 1; ++q) all_ok = all_ok && (!ready || peer_flag[q] == 0);
     // Items (owned row, RW-column run), rows fastest: a warp's 16-byte
     // loads of one run cover consecutive rows.  Runs are 32 columns, or 16
     // when bn is not a multiple of 32 (a 32-column run could then straddle
@@ -883,9 +896,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       sum_pass(std::integral_constant<int, 16>{});
   }
   __syncthreads();
-  // No CTA leaves while a store into its shared memory may be in flight:
-  // every owner has seen its partials land before this barrier.
-  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
