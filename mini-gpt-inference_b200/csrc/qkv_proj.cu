@@ -565,18 +565,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // The x box is only as tall as the live tokens (rows of the A operand past
 // it hold stale data, which only reaches accumulator rows that are never
 // stored).  The live token rows are divided into `splits` contiguous
-// ranges of `per` rows, CTA r owning range r.  Once every CTA of the
-// cluster has its accumulator (a cluster barrier: every ring is idle),
-// each thread reads its TMEM row and writes it to the row's owner: into
+// ranges of `per` rows, CTA r owning range r.  Once this CTA's accumulator
+// is complete, each thread reads its TMEM row and writes it to the row's
+// owner: into
 // its own staging rows, or with st.async into the owner's receive slot for
 // this CTA, completing as transaction bytes on the owner's recv_full
-// barrier; each sender's abort flag travels the same way.  The owner then
+// barrier; each sender's abort flag travels the same way.  The receive
+// slots sit after the operand ring, so a CTA sends as soon as its own
+// accumulator is complete, without waiting for its peers'.  The owner then
 // sums its rows' partials in rank order (the same order every run) from
 // its own shared memory, rounds once to bf16 and stores 32- (or 16-)
 // column runs; the (row, run) items are spread over all of the CTA's
-// threads.  The slot of each owned row is read while the MMAs run.  After
-// the one cluster barrier no CTA reads another's shared memory, and every
-// CTA written to waits for its bytes, so no barrier is needed at the end.
+// threads.  The slot of each owned row is read while the MMAs run.  No CTA
+// reads another's shared memory, and every CTA written to waits for its
+// bytes, so no barrier is needed at the end.
 constexpr int kSplitMaxBN = 256;
 // A stage holds kc (1 or 2) consecutive 64-column chunks of x and W,
 // fetched by one 3-D box per operand ({64 columns, rows, chunks}; the chunk
@@ -594,14 +596,6 @@ constexpr int kSplitBytes = kSplitSlotOffset + kBM * 8;
 constexpr int kSplitMaxCluster = 8;  // splits per cluster
 static_assert((2 * kSplitMaxStages + 3) * 8 + 8 + 4 * kSplitMaxCluster <= 512, "barrier area too small");
 
-// Bytes of the reduction area for `rows` live token rows: this CTA's own
-// rows, then a receive slot per peer, ceil(rows / splits) rows each.  Rows
-// are bn + 4 floats apart: 16-byte aligned, and the 16-byte accesses of a
-// warp's 32 consecutive rows fall in distinct banks.
-__host__ __device__ constexpr int64_t split_reduce_bytes(int rows, int bn, int splits) {
-  return static_cast<int64_t>(splits) * ((rows + splits - 1) / splits) * (bn + 4) * 4;
-}
-
 struct SplitShape {
   int bn;           // output features per tile (multiple of 16, <= 256)
   int xrows;        // x box rows (multiple of 8, <= 128)
@@ -610,7 +604,30 @@ struct SplitShape {
   int stages;
   int splits;
   int kpb;          // k-steps per split
+  int recv_off;     // byte offset of the receive slots after the ring, or 0:
+                    // the slots follow this CTA's own rows in the ring
 };
+
+// Bytes of the receive slots of a split plan (a multiple of 1024): per
+// peer, ceil(rows / splits) rows of bn + 4 floats.  Where they fit without
+// costing the operand ring a stage they sit after it, so peers may write
+// them while this CTA's MMAs still run; otherwise they follow this CTA's
+// own rows in the ring, written once every CTA of the cluster is done.
+int64_t split_recv_bytes(int rows, int bn, int splits) {
+  const int64_t b = static_cast<int64_t>(splits - 1) * ((rows + splits - 1) / splits) * (bn + 4) * 4;
+  return (b + 1023) / 1024 * 1024;
+}
+
+// A split plan fits when this CTA's own rows and the receive slots fit the
+// reduction area (the slots may have to share the ring), and the ring holds
+// at least two one-chunk stages (plus the M = 128 MMA's 16 KB A window past
+// the last one).
+bool split_fits(int rows, int bn, int splits) {
+  const int64_t own = static_cast<int64_t>((rows + splits - 1) / splits) * (bn + 4) * 4;
+  const int64_t stage = static_cast<int64_t>(rows + bn) * 128;
+  return own + split_recv_bytes(rows, bn, splits) <= kSplitAreaBytes &&
+         (kSplitAreaBytes - kBM * 128) / stage + 1 >= 2;
+}
 
 // 16-byte store into a cluster peer's shared memory, counted as 16
 // transaction bytes on the peer's mbarrier (both shared::cluster addresses).
@@ -677,6 +694,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Receive slots after the ring: every CTA of the cluster arrives once its
+  // barriers exist and waits (below) before writing into a peer's shared
+  // memory.  In the ring: one full cluster barrier after the MMAs.
+  const bool early = sh.recv_off != 0;
+  if (early) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const int tile = blockIdx.x / splits;
   const int m0 = (tile % p.m_tiles) * kBM;
@@ -689,16 +711,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // acc_row gives the row that lane `lane` of lane quarter q holds (-1: none).
   const int mma_m = sh.xrows <= 64 ? 64 : kBM;
   auto acc_row = [&](int q, int ln) { return mma_m == 64 ? (ln < 16 ? q * 16 + ln : -1) : q * 32 + ln; };
-  // Reduction rows, over the ring once the MMAs are done: this CTA's own
-  // rows at (row - own_lo) * rs floats, then the receive slots, `per` rows
-  // per sender (sender q's slot is q, or q - 1 past this CTA's rank).
+  // Reduction rows: this CTA's own rows over the ring once its MMAs are
+  // done, at (row - own_lo) * rs floats; the receive slots after the ring,
+  // `per` rows per sender (sender q's slot is q, or q - 1 past this CTA's
+  // rank).
+  // Rows are bn + 4 floats apart: 16-byte aligned, and the 16-byte accesses
+  // of a warp's 32 consecutive rows fall in distinct banks.
   const int rs = bn + 4;
   const int per = (live + splits - 1) / splits;
   auto own_lo = [&](int q) { return min(live, q * per); };
   auto own_n = [&](int q) { return min(live, q * per + per) - min(live, q * per); };
   auto slot_of = [&](int sender, int owner) { return sender < owner ? sender : sender - 1; };
   float* stage_rows = reinterpret_cast<float*>(smem);
-  float* recv_rows = stage_rows + per * rs;
+  float* recv_rows = early ? reinterpret_cast<float*>(smem + sh.recv_off) : stage_rows + per * rs;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -777,7 +802,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
-  cluster_sync_all();  // every accumulator of the cluster is complete and every ring idle
+  if (early)
+    // Every peer's barriers exist (arrived long ago: this does not wait for
+    // the peers' MMAs; the receive slots are not part of the ring).
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  else
+    cluster_sync_all();  // every CTA's MMAs are done and its ring idle
   if (warp >= 2) {
     // Each thread sends its TMEM row to the row's owner; the thread holding
     // an owner's first row also sends this CTA's abort flag.  A CTA whose
@@ -1080,18 +1110,31 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
   // The M = 128 MMA reads 16 KB of A rows from each chunk's base, past the
   // chunk when the x box is short: the last stage's last A window must
   // still end inside the ring.
-  auto ring_stages = [&](int kc) {
-    const int sb = kc * (sh.xrows + sh.bn) * 128;
-    return std::min({kSplitMaxStages, kSplitAreaBytes / sb,
-                     (kSplitAreaBytes - kBM * 128 - (kc - 1) * sh.xrows * 128) / sb + 1});
-  };
-  sh.kc = ring_stages(2) >= 3 ? 2 : 1;
-  sh.stage_bytes = sh.kc * (sh.xrows + sh.bn) * 128;
-  sh.stages = ring_stages(sh.kc);
   sh.splits = plan.splits;
-  if (sh.splits < 1 || sh.splits > 8 ||
-      split_reduce_bytes(sh.xrows, sh.bn, sh.splits) > kSplitAreaBytes)
+  if (sh.splits < 1 || sh.splits > kSplitMaxCluster || !split_fits(sh.xrows, sh.bn, sh.splits))
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: split plan exceeds the reduction area");
+  // Ring stages for a ring of ring_bytes; the receive slots go after the
+  // ring when that costs it neither a stage nor its two-chunk stages.
+  auto ring_stages = [&](int ring_bytes, int kc) {
+    const int sb = kc * (sh.xrows + sh.bn) * 128;
+    return std::min({kSplitMaxStages, ring_bytes / sb,
+                     (ring_bytes - kBM * 128 - (kc - 1) * sh.xrows * 128) / sb + 1});
+  };
+  auto ring_shape = [&](int ring_bytes, int& kc, int& stages) {
+    kc = ring_stages(ring_bytes, 2) >= 3 ? 2 : 1;
+    stages = ring_stages(ring_bytes, kc);
+  };
+  int kc_full, stages_full, kc_short, stages_short;
+  const int short_ring = kSplitAreaBytes - static_cast<int>(split_recv_bytes(sh.xrows, sh.bn, sh.splits));
+  ring_shape(kSplitAreaBytes, kc_full, stages_full);
+  ring_shape(short_ring, kc_short, stages_short);
+  const bool after = sh.splits > 1 && kc_short == kc_full && stages_short == stages_full;
+  sh.kc = after ? kc_short : kc_full;
+  sh.stages = after ? stages_short : stages_full;
+  sh.recv_off = after ? short_ring : 0;
+  sh.stage_bytes = sh.kc * (sh.xrows + sh.bn) * 128;
+  if (sh.stages < 2)
+    return fail(B200_ERR_UNSUPPORTED, "qkv projection: split plan leaves too small an operand ring");
   CUtensorMap tx, tw;
   {
     // {64 columns, token rows, 64-column chunks}: the chunk dimension
@@ -1168,7 +1211,7 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
       const int64_t tiles = m_tiles * ceil_div(3 * C, bn);
       for (int s = 1; s <= 8; ++s) {
         if (tiles * s > num_sms || (s > 1 && k_iters / s < 8)) continue;
-        if (split_reduce_bytes(xrows, bn, s) > kSplitAreaBytes) continue;
+        if (!split_fits(xrows, bn, s)) continue;
         if (s > 1 && tiles > split_capacity(s, dev)) continue;
         const int64_t cost = ceil_div(k_iters, s) * (xrows + bn);
         if (best_cost < 0 || cost < best_cost) {
