@@ -75,6 +75,8 @@ def _check_pool(c, y, status_bits=0):
     (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (split-K clusters)
     (96, 4096, 32, 16, 1, 0),    # split-K clusters, 48 rows owned per cluster rank
     (77, 4096, 32, 16, 1, 0),    # split-K clusters, ragged owned rows (39 + 38)
+    (1, 2048, 16, 16, 1, 0),     # split-K clusters of more than 2 CTAs (hidden 2048)
+    (37, 2048, 16, 16, 2, 1),    # clusters of more than 2 CTAs, ragged owned rows
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
     (100, 1024, 8, 16, 1, 0),    # split-K clusters at hidden 1024 (16 k-steps)
     (129, 4096, 32, 16, 2, 1),   # CTA pairs (192-wide tiles); the second CTA holds one token
@@ -235,6 +237,19 @@ def test_qkv_kv_write_full_size_against_cublas():
     yk, yv = y[sample, C:2 * C].float(), y[sample, 2 * C:].float()
     assert ((kf - yk).abs() <= yk.abs() * ulp + 1e-3).all()
     assert ((vf - yv).abs() <= yv.abs() * ulp + 1e-3).all()
+
+
+@pytest.mark.parametrize("T,C", [(1, 2048), (37, 2048)])
+def test_qkv_plan_splits_over_more_than_two_ctas(T, C):
+    """The parity cases at hidden 2048 reach split-K clusters of 3+ CTAs."""
+    import ctypes
+
+    from b200attn import _lib
+
+    lib = _lib.load()
+    k, n, s = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    assert lib.b200_qkv_kv_write_plan(T, C, ctypes.byref(k), ctypes.byref(n), ctypes.byref(s)) == 0
+    assert k.value == 2 and s.value >= 3, (k.value, n.value, s.value)
 
 
 @pytest.mark.parametrize("T,C,kind", [
