@@ -324,7 +324,28 @@ class ScatterWorkload:
                 "parallelism": f"token-sharded dp{world}"}
 
     def extra(self, value, ms_max, world, steps):
-        return {}
+        """A plain device copy of the same bytes (k and v into fresh tensors,
+        torch ``copy_``), timed like the steps: the bandwidth a copy of this
+        size reaches, below the measured peak, which comes from a 4 GB copy."""
+        kd, vd = torch.empty_like(self.kn), torch.empty_like(self.vn)
+
+        def copy():
+            kd.copy_(self.kn)
+            vd.copy_(self.vn)
+
+        for _ in range(3):
+            copy()
+        torch.cuda.synchronize(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            copy()
+        e1.record()
+        torch.cuda.synchronize(self.device)
+        ms = e0.elapsed_time(e1) / steps
+        moved = 2 * (kd.numel() + vd.numel()) * kd.element_size()
+        return {"same_bytes_copy": {"ms_per_step": round(ms, 5), "GB/s": round(moved / ms / 1e6, 1),
+                                    "bytes": moved}}
 
 
 class QkvWorkload:
