@@ -57,6 +57,18 @@ constexpr int kBM = 128;                 // tokens per tile (TMEM lanes)
 constexpr int kBK = 64;                  // reduction elements per stage (one 128-byte row)
 constexpr int kThreads = 192;            // producer, MMA issuer, 4 epilogue warps
 constexpr int kRingBytes = 192 * 1024;   // operand ring (1 CTA per SM)
+// Epilogue stores of the tile kernels.  An epilogue warp holds 32 token
+// rows of an accumulator, one per lane; stored from registers, each 16-byte
+// store of the warp would touch 32 rows (32 memory requests per
+// instruction).  Instead each 64-column batch is rounded to bf16, written
+// to the warp's staging rows in shared memory and read back so that 8
+// consecutive lanes store one row's 128 contiguous bytes: 4 rows, whole
+// lines, per instruction.  Staging rows are kEpiPitch = 128 + 16 bytes
+// apart, so both the row-wise writes and the line-wise reads of 8 lanes
+// fall in distinct banks.
+constexpr int kEpiPitch = 144;
+constexpr int kEpiWarpBytes = 32 * kEpiPitch;
+constexpr int kEpiBytes = 4 * kEpiWarpBytes;  // the four epilogue warps
 
 template <int BN>
 struct QkvCfg {
@@ -65,7 +77,8 @@ struct QkvCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = kRingBytes / STAGE;  // 6 / 8 for BN 128 / 64
   static constexpr int BAR = STAGES * STAGE;
-  static constexpr int BYTES = BAR + 256;
+  static constexpr int EPI = BAR + 256;  // the epilogue warps' staging rows
+  static constexpr int BYTES = EPI + kEpiBytes;
   static constexpr int TMEM_COLS = 2 * BN;  // two f32 accumulators
   static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
   static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area too small");
@@ -111,7 +124,46 @@ __device__ __forceinline__ void store_run(__nv_bfloat16* dst, const float* v) {
     d[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
                       pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
 }
-__device__ __forceinline__ void store_run32(__nv_bfloat16* dst, const float* v) { store_run<32>(dst, v); }
+
+// Destination of columns [n, n + 64) of token row `row`, or nullptr when
+// they are not stored (a row past the tokens, columns past 3C, a bad
+// slot).  n and C are multiples of 64, so the run lies in one of q, k, v;
+// dst_row is the token's first element in the layer's pool rows (< 0: no
+// slot).
+__device__ __forceinline__ __nv_bfloat16* epi_dst(const QkvParams& p, bool live, int64_t row,
+                                                  int64_t dst_row, int64_t n) {
+  if (!live || n >= 3 * p.C) return nullptr;
+  if (n < p.C) return p.q_out + row * p.q_rs + n;
+  if (dst_row < 0) return nullptr;
+  return n < 2 * p.C ? p.k_pool + dst_row + (n - p.C) : p.v_pool + dst_row + (n - 2 * p.C);
+}
+
+// Loads 64 accumulator columns at TMEM address `taddr` (this warp's lane
+// quarter) and stores lane l's row to dst (per lane; nullptr: skipped)
+// through the warp's staging rows `stage`.  Warp-collective.
+__device__ __forceinline__ void epi_store64(uint32_t taddr, uint8_t* stage, __nv_bfloat16* dst,
+                                            int lane) {
+  float v[64];
+  __syncwarp();  // tcgen05.ld is warp-collective; the staging rows are free
+  tmem_ld32(taddr, v);
+  tmem_ld32(taddr + 32u, v + 32);
+  tmem_wait_ld();
+  uint4* srow = reinterpret_cast<uint4*>(stage + lane * kEpiPitch);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    srow[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                         pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+  __syncwarp();
+  const unsigned long long d = reinterpret_cast<unsigned long long>(dst);
+  const int part = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = (lane >> 3) + 4 * i;
+    const unsigned long long rd = __shfl_sync(0xffffffffu, d, r);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * kEpiPitch + part * 16);
+    if (rd != 0ull) reinterpret_cast<uint4*>(rd)[part] = val;
+  }
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -134,6 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int32_t* abort_v = abort_flag;
 
   if (threadIdx.x == 0) {
+    // The tensor maps are fetched while the barriers and TMEM are set up.
+    tma_prefetch_desc(&tmx);
+    tma_prefetch_desc(&tmw);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -162,8 +217,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmx);
-      tma_prefetch_desc(&tmw);
       int64_t issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
@@ -254,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // cover quarters 2, 3, 0, 1.
     const int qd = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    uint8_t* stage = smem + Cfg::EPI + qd * kEpiWarpBytes;
     int i = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const int acc = i & 1;
@@ -282,25 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
+      // BN and n0 are multiples of 64: every batch lies in one of q, k, v.
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        __syncwarp();  // tcgen05.ld is warp-collective
-        tmem_ld32(tacc + static_cast<uint32_t>(c), v);
-        tmem_wait_ld();
-        const int64_t n = n0 + c;
-        if (live && n < 3 * p.C) {
-          if (n < p.C) {
-            store_run32(p.q_out + row * p.q_rs + n, v);
-          } else if (dst_row >= 0) {
-            // C is a multiple of 64, so a 32-column run never straddles thirds.
-            if (n < 2 * p.C)
-              store_run32(p.k_pool + dst_row + (n - p.C), v);
-            else
-              store_run32(p.v_pool + dst_row + (n - 2 * p.C), v);
-          }
-        }
-      }
+      for (int c = 0; c < BN; c += 64)
+        epi_store64(tacc + static_cast<uint32_t>(c), stage, epi_dst(p, live, row, dst_row, n0 + c), lane);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
     }
@@ -339,7 +378,8 @@ struct PairCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = kRingBytes / STAGE;  // 6
   static constexpr int BAR = STAGES * STAGE;
-  static constexpr int BYTES = BAR + 256;
+  static constexpr int EPI = BAR + 256;  // the epilogue warps' staging rows
+  static constexpr int BYTES = EPI + kEpiBytes;
   static constexpr int TMEM_COLS = 512;            // two BN-column accumulators (a power of 2)
   static_assert(2 * BN <= TMEM_COLS, "two accumulators must fit the allocation");
   static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
@@ -368,6 +408,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   volatile int32_t* abort_v = abort_flag;
 
   if (threadIdx.x == 0) {
+    // The tensor maps are fetched while the barriers and TMEM are set up.
+    tma_prefetch_desc(&tmx);
+    tma_prefetch_desc(&tmw);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -401,8 +444,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producers (both CTAs)
     if (lane == 0) {
-      tma_prefetch_desc(&tmx);
-      tma_prefetch_desc(&tmw);
       const uint32_t full0 = map_to_rank(full, 0);
       int64_t issued = 0;
       bool ok = true;
@@ -489,6 +530,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int qd = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    uint8_t* stage = smem + Cfg::EPI + qd * kEpiWarpBytes;
     const uint32_t acc_empty0 = map_to_rank(acc_empty, 0);
     int i = 0;
     for (int t = pair; t < ntiles; t += npairs, ++i) {
@@ -518,23 +560,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        __syncwarp();
-        tmem_ld32(tacc + static_cast<uint32_t>(c), v);
-        tmem_wait_ld();
-        const int64_t n = n0 + c;
-        if (live && n < 3 * p.C) {
-          if (n < p.C) {
-            store_run32(p.q_out + row * p.q_rs + n, v);
-          } else if (dst_row >= 0) {
-            if (n < 2 * p.C)
-              store_run32(p.k_pool + dst_row + (n - p.C), v);
-            else
-              store_run32(p.v_pool + dst_row + (n - 2 * p.C), v);
-          }
-        }
-      }
+      for (int c = 0; c < BN; c += 64)
+        epi_store64(tacc + static_cast<uint32_t>(c), stage, epi_dst(p, live, row, dst_row, n0 + c), lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc_empty0 + static_cast<uint32_t>(acc * 8));
@@ -674,6 +701,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   int64_t* row_slot = reinterpret_cast<int64_t*>(smem + kSplitSlotOffset);  // [kBM]
 
   if (threadIdx.x == 0) {
+    // The tensor maps are fetched while the barriers and TMEM are set up.
+    tma_prefetch_desc(&tmx);
+    tma_prefetch_desc(&tmw);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -727,8 +757,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tmx);
-      tma_prefetch_desc(&tmw);
       // Every CTA of a split reads the same x columns; starting each tile's
       // walk at its own k-step spreads those reads over the L2 slices
       // instead of all CTAs requesting one chunk at a time.
