@@ -96,6 +96,7 @@ struct QkvParams {
   int64_t nslots;   // P * S
   int32_t slots_i64;
   int32_t m_tiles, n_tiles, k_iters;
+  int32_t pair_rows;  // CTA pairs: token rows per CTA of a tile (128, or fewer for one short tile)
   int32_t* status;
 };
 
@@ -357,8 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ CTA pairs
 // For long token runs the tiles are 256 tokens x BN features, computed by
 // a cluster of two CTAs with tcgen05.mma.cta_group::2: CTA r of the pair
-// loads token rows [128r, +128) of the x tile and feature rows
-// [BN/2 * r, +BN/2) of the W tile, and the pair MMA (issued by CTA 0 only)
+// loads token rows [128r, +128) of the x tile (a single tile of at most 256
+// tokens is split evenly instead: `pair_rows` rows per CTA, the A rows past
+// them left stale, reaching only accumulator rows that are never stored)
+// and feature rows [BN/2 * r, +BN/2) of the W tile, and the pair MMA (issued by CTA 0 only)
 // multiplies the pair's 256 x rows by all BN W rows, each CTA's TMEM receiving the
 // accumulator rows of its own tokens.  Per SM this halves the W bytes
 // staged in shared memory for the same tensor work, which a single CTA
@@ -450,7 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = pair; ok && t < ntiles; t += npairs) {
         int mt, nt;
         tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
-        const int m0 = mt * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int m0 = mt * 2 * kBM + static_cast<int>(rank) * p.pair_rows;
         const int n0 = nt * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < p.k_iters; ++kb) {
           const int st = static_cast<int>(issued % STAGES);
@@ -460,7 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           // CTA 0's stage barrier counts the bytes of both CTAs' copies.
-          if (rank == 0) mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(2 * Cfg::STAGE));
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2u * static_cast<uint32_t>(p.pair_rows * 128 + Cfg::B_BYTES));
           uint8_t* a = smem + st * Cfg::STAGE;
           const uint32_t bar = full0 + static_cast<uint32_t>(st * 8);
           tma_load_2d_pair(a, &tmx, bar, kb * kBK, m0);
@@ -546,9 +549,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int mt, nt;
       tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
-      const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + qd * 32 + lane;
+      const int lr = qd * 32 + lane;  // accumulator row (TMEM lane) of this CTA
+      const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * p.pair_rows + lr;
       const int64_t n0 = static_cast<int64_t>(nt) * BN;
-      const bool live = row < p.T;
+      const bool live = lr < p.pair_rows && row < p.T;
       int64_t dst_row = -1;
       if (live && n0 + BN > p.C) {
         const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
@@ -1046,8 +1050,12 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
   const size_t smem = static_cast<size_t>(Cfg::BYTES) + 1024;
   if (smem > static_cast<size_t>(dev.max_smem_optin))
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
+  // One tile of at most 256 tokens: each CTA takes half of the tokens
+  // (rounded up to 8 rows) so that neither stages more x rows than needed.
+  const int rows = T <= 2 * kBM ? static_cast<int>(std::min<int64_t>(kBM, (ceil_div(T, 2) + 7) / 8 * 8))
+                                : kBM;
   CUtensorMap tx, tw;
-  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
+  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, rows);
   if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, BN / 2);  // this CTA's half
   if (rc != B200_OK) return rc;
   static std::atomic<int> max_pairs[64];
@@ -1073,7 +1081,8 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
     }
     pairs = max_pairs[dev.device].load(std::memory_order_acquire);
   }
-  const QkvParams prm = make_params(a, 2 * kBM, BN, kBK);
+  QkvParams prm = make_params(a, 2 * kBM, BN, kBK);
+  prm.pair_rows = rows;
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, pairs));
   qkv_kv_write_pair_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);

@@ -79,7 +79,8 @@ def _check_pool(c, y, status_bits=0):
     (37, 2048, 16, 16, 2, 1),    # clusters of more than 2 CTAs, ragged owned rows
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
     (100, 1024, 8, 16, 1, 0),    # split-K clusters at hidden 1024 (16 k-steps)
-    (129, 4096, 32, 16, 2, 1),   # CTA pairs (192-wide tiles); the second CTA holds one token
+    (129, 4096, 32, 16, 2, 1),   # CTA pairs (192-wide tiles), 72 + 57 token rows per pair
+    (161, 4096, 32, 16, 1, 0),   # CTA pairs, 88 + 73 token rows (rows past them stale, not stored)
     (128, 4096, 32, 16, 1, 0),   # single CTAs, 128-wide tiles, one wave
     (256, 4096, 32, 16, 1, 0),   # CTA pairs, 192-wide tiles, one wave
     (300, 512, 4, 16, 1, 0),     # single CTAs, 64-wide tiles
@@ -87,7 +88,7 @@ def _check_pool(c, y, status_bits=0):
     (600, 2048, 16, 16, 2, 1),   # CTA pairs; the second CTA of the last pair has no rows
     (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step, ragged 128-wide tile
     (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
-    (200, 3136, 49, 16, 1, 0),   # 3C = 36.75 x 256: ragged last output tile
+    (200, 3136, 49, 16, 1, 0),   # hidden 3136 (49 heads of 64): 49 pairs of 192-wide tiles
     (200, 4160, 65, 16, 1, 0),   # CTA pairs, 192-wide tiles, 65 pairs
     (200, 6400, 50, 16, 1, 0),   # more tiles than SMs: single CTAs, 128-wide tiles, 3 waves
     (1000, 4160, 65, 16, 1, 0),  # CTA pairs, 3C = 48.75 tiles: ragged last output tile
