@@ -352,7 +352,13 @@ class QkvWorkload:
     """The attention's QKV projection with the KV write in its epilogue
     (b200_qkv_kv_write), bf16, hidden 4096 (H=32, D=128): a prefill batch
     of 16 x 512 tokens (tensor-bound) or a decode batch of 64 tokens
-    (bound by the 100 MB weight read)."""
+    (bound by the 100 MB weight read).  Step i projects with layer i % LAYERS
+    of LAYERS weight matrices and writes that layer's pool rows, as a
+    model's forward does: 403 MB of weights, so no step finds its weights
+    in the 126 MB L2 (one 100 MB matrix reused every step would mostly
+    stay there)."""
+
+    LAYERS = 4
 
     def __init__(self, name, rank, device):
         self.name, self.device = name, device
@@ -363,11 +369,12 @@ class QkvWorkload:
         g = torch.Generator().manual_seed(rank)
         gd = torch.Generator(device=device).manual_seed(40260000 + rank)
         P = T // S * 2
-        self.k = torch.zeros((1, P, S, H, D), dtype=torch.bfloat16, device=device)
+        self.k = torch.zeros((self.LAYERS, P, S, H, D), dtype=torch.bfloat16, device=device)
         self.v = torch.zeros_like(self.k)
         self.pool = SimpleNamespace(k=self.k, v=self.v, block_size=S)
-        self.w = (torch.empty((3 * C, C), dtype=torch.bfloat16, device=device)
-                  .normal_(0.0, 0.02, generator=gd))
+        self.ws = [torch.empty((3 * C, C), dtype=torch.bfloat16, device=device)
+                   .normal_(0.0, 0.02, generator=gd) for _ in range(self.LAYERS)]
+        self.i = self.j = 0
         self.x_h = torch.randn((T, C), generator=g).to(torch.bfloat16).pin_memory()
         self.slots_h = torch.randperm(P * S, generator=g)[:T].pin_memory()
         self.x, self.slots = self.x_h.to(device), self.slots_h.to(device)
@@ -377,15 +384,19 @@ class QkvWorkload:
 
     def prepare(self):
         from b200attn import qkv_kv_write_b200
-        self.call = qkv_kv_write_b200(self.x, self.w, self.pool, self.slots, 0, prepare=True)
+        self.calls = [qkv_kv_write_b200(self.x, w, self.pool, self.slots, layer, prepare=True)
+                      for layer, w in enumerate(self.ws)]
 
     def step(self):
-        self.call()
+        self.calls[self.i % self.LAYERS]()
+        self.i += 1
 
     def e2e_step(self):
         from b200attn import qkv_kv_write_b200
-        q = qkv_kv_write_b200(self.x_h.to(self.device, non_blocking=True), self.w, self.pool,
-                              self.slots_h.to(self.device, non_blocking=True), 0)
+        layer = self.j % self.LAYERS
+        self.j += 1
+        q = qkv_kv_write_b200(self.x_h.to(self.device, non_blocking=True), self.ws[layer], self.pool,
+                              self.slots_h.to(self.device, non_blocking=True), layer)
         self.q_h.copy_(q.view(self.T, self.C), non_blocking=True)
 
     def flops(self) -> float:
@@ -407,30 +418,37 @@ class QkvWorkload:
     def config(self, world):
         return {"workload": self.desc, "tokens_per_gpu": self.T, "hidden": self.C, "heads": H,
                 "head_dim": D, "block_size": S, "accumulate": "f32",
-                "l2": "weights %.0f MB, no flush between steps" % (3 * self.C * self.C * 2 / 1e6),
+                "l2": "%d weight matrices of %.0f MB cycled step by step (%.0f MB, larger than L2);"
+                      " no flush" % (self.LAYERS, 3 * self.C * self.C * 2 / 1e6,
+                                     self.LAYERS * 3 * self.C * self.C * 2 / 1e6),
                 "parallelism": f"token-sharded dp{world}"}
 
     def extra(self, value, ms_max, world, steps):
         """The unfused sequence the kernel replaces, timed the same way:
         torch's bf16 matmul (cuBLAS) into a [T, 3C] tensor, then the
-        slot-mapping scatter of its k and v thirds (a prepared call).  The
-        ``cuda_graph`` entry times the fused call and both unfused sequences
-        as CUDA graphs of 10 calls, device time without host overhead, which
-        at decode sizes is larger than the kernels themselves."""
+        slot-mapping scatter of its k and v thirds (a prepared call), cycling
+        over the layers like the steps.  The ``cuda_graph`` entry times the
+        fused call and both unfused sequences as CUDA graphs of 12 calls
+        (three passes over the layers), device time without host overhead,
+        which at decode sizes is larger than the kernels themselves."""
         from b200attn import kv_scatter_b200
         T, C = self.T, self.C
         dev = self.device
         y = torch.empty((T, 3 * C), dtype=torch.bfloat16, device=dev)
         with torch.inference_mode():
-            scatter_call = kv_scatter_b200(y[:, C:2 * C].view(T, H, D), y[:, 2 * C:].view(T, H, D),
-                                           self.pool, self.slots, 0, prepare=True)
+            scatter_calls = [kv_scatter_b200(y[:, C:2 * C].view(T, H, D), y[:, 2 * C:].view(T, H, D),
+                                             self.pool, self.slots, layer, prepare=True)
+                             for layer in range(self.LAYERS)]
+        turn = [0]
 
         def unfused(scatter):
-            torch.matmul(self.x, self.w.t(), out=y)
+            layer = turn[0] % self.LAYERS
+            turn[0] += 1
+            torch.matmul(self.x, self.ws[layer].t(), out=y)
             if scatter:
-                scatter_call()
+                scatter_calls[layer]()
 
-        def graph_ms(fn, calls=10, reps=20):
+        def graph_ms(fn, calls=12, reps=20):
             side = torch.cuda.Stream(dev)
             side.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(side):
@@ -470,7 +488,7 @@ class QkvWorkload:
                 res[key] = {"ms_per_step": ms,
                             "value": self.work() / (ms * 1e-3) / (1e12 if self.bound == "tensor" else 1e9),
                             "unit": self.unit}
-            res["cuda_graph"] = {"fused_ms_per_call": graph_ms(self.call),
+            res["cuda_graph"] = {"fused_ms_per_call": graph_ms(self.step),
                                  "cublas_matmul_alone_ms_per_call": graph_ms(lambda: unfused(False)),
                                  "cublas_matmul_plus_scatter_ms_per_call": graph_ms(lambda: unfused(True))}
         res["fused_ms_per_step"] = ms_max / steps
