@@ -96,7 +96,7 @@ struct QkvParams {
   int64_t nslots;   // P * S
   int32_t slots_i64;
   int32_t m_tiles, n_tiles, k_iters;
-  int32_t pair_rows;  // CTA pairs: token rows per CTA of a tile (128, or fewer for one short tile)
+  int32_t x_rows;  // token rows per x box of a CTA (128, or fewer for one short tile)
   int32_t* status;
 };
 
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(Cfg::STAGE));
+          mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(p.x_rows * 128 + Cfg::B_BYTES));
           uint8_t* a = smem + st * Cfg::STAGE;
           tma_load_2d(a, &tmx, &full[st], kb * kBK, m0);
           tma_load_2d(a + Cfg::A_BYTES, &tmw, &full[st], kb * kBK, n0);
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // For long token runs the tiles are 256 tokens x BN features, computed by
 // a cluster of two CTAs with tcgen05.mma.cta_group::2: CTA r of the pair
 // loads token rows [128r, +128) of the x tile (a single tile of at most 256
-// tokens is split evenly instead: `pair_rows` rows per CTA, the A rows past
+// tokens is split evenly instead: `x_rows` rows per CTA, the A rows past
 // them left stale, reaching only accumulator rows that are never stored)
 // and feature rows [BN/2 * r, +BN/2) of the W tile, and the pair MMA (issued by CTA 0 only)
 // multiplies the pair's 256 x rows by all BN W rows, each CTA's TMEM receiving the
@@ -453,7 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = pair; ok && t < ntiles; t += npairs) {
         int mt, nt;
         tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
-        const int m0 = mt * 2 * kBM + static_cast<int>(rank) * p.pair_rows;
+        const int m0 = mt * 2 * kBM + static_cast<int>(rank) * p.x_rows;
         const int n0 = nt * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < p.k_iters; ++kb) {
           const int st = static_cast<int>(issued % STAGES);
@@ -463,7 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           // CTA 0's stage barrier counts the bytes of both CTAs' copies.
-          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2u * static_cast<uint32_t>(p.pair_rows * 128 + Cfg::B_BYTES));
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2u * static_cast<uint32_t>(p.x_rows * 128 + Cfg::B_BYTES));
           uint8_t* a = smem + st * Cfg::STAGE;
           const uint32_t bar = full0 + static_cast<uint32_t>(st * 8);
           tma_load_2d_pair(a, &tmx, bar, kb * kBK, m0);
@@ -550,9 +550,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int mt, nt;
       tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
       const int lr = qd * 32 + lane;  // accumulator row (TMEM lane) of this CTA
-      const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * p.pair_rows + lr;
+      const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * p.x_rows + lr;
       const int64_t n0 = static_cast<int64_t>(nt) * BN;
-      const bool live = lr < p.pair_rows && row < p.T;
+      const bool live = lr < p.x_rows && row < p.T;
       int64_t dst_row = -1;
       if (live && n0 + BN > p.C) {
         const int64_t slot = load_index(p.slots, row * p.ss, p.slots_i64);
@@ -1021,8 +1021,11 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
   if (smem > static_cast<size_t>(dev.max_smem_optin))
     return fail(B200_ERR_UNSUPPORTED, "qkv projection: not enough shared memory");
 
+  // A single token tile stages only its live rows (rounded up to 8): the A
+  // rows past them are stale and reach only accumulator rows never stored.
+  const int rows = T < kBM ? static_cast<int>((T + 7) / 8 * 8) : kBM;
   CUtensorMap tx, tw;
-  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, kBM);
+  int rc = encode_rows(&tx, a.x, T, C, a.x_row_stride, rows);
   if (rc == B200_OK) rc = encode_rows(&tw, a.weight, 3 * C, C, C, BN);
   if (rc != B200_OK) return rc;
   static std::atomic<int> configured[64];
@@ -1034,7 +1037,8 @@ int launch_bn(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Devi
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(qkv_kv_write)");
     configured[dev.device].store(1, std::memory_order_release);
   }
-  const QkvParams prm = make_params(a, kBM, BN, kBK);
+  QkvParams prm = make_params(a, kBM, BN, kBK);
+  prm.x_rows = rows;
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.num_sms));
   qkv_kv_write_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);
@@ -1082,7 +1086,7 @@ int launch_pair(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const De
     pairs = max_pairs[dev.device].load(std::memory_order_acquire);
   }
   QkvParams prm = make_params(a, 2 * kBM, BN, kBK);
-  prm.pair_rows = rows;
+  prm.x_rows = rows;
   const int64_t tiles = static_cast<int64_t>(prm.m_tiles) * prm.n_tiles;
   const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, pairs));
   qkv_kv_write_pair_kernel<BN><<<grid, kThreads, smem, stream>>>(tx, tw, prm);
@@ -1221,13 +1225,14 @@ int launch_split(const b200_qkv_kv_write_args_t& a, cudaStream_t stream, const Q
 QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
-  if (m_tiles <= 2 && T > 120) {
-    // 121..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
+  if (m_tiles <= 2 && T > 96) {
+    // 97..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
     // BN) beats split-K clusters once those tiles fit in one wave: at
-    // hidden 4096, 128 tokens take 23.0 us on single CTAs against 23.6 us
-    // split-K, and 256 tokens 26.9 us on 192-wide CTA pairs against 33.6 us
-    // (112 tokens: 21.7 us split-K, 22.6 us single CTAs).  Pairs take
-    // 192-wide tiles when those fit one wave too: more SMs, fewer bytes each.
+    // hidden 4096 with every call on another layer's weights, 104-128 tokens
+    // take 24.2-24.3 us on single CTAs against 24.6-25.5 us split-K (96
+    // tokens: 24.1 against 24.3, level), and 256 tokens 27.0 us on 192-wide
+    // CTA pairs against 33 us.  Pairs take 192-wide tiles when those fit
+    // one wave too: more SMs, fewer bytes each.
     const int64_t single_tiles = ceil_div(3 * C, 128);
     if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
     if (m_tiles == 2 && ceil_div(3 * C, kPairBNNarrow) <= num_sms / 2)

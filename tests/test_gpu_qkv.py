@@ -78,7 +78,8 @@ def _check_pool(c, y, status_bits=0):
     (1, 2048, 16, 16, 1, 0),     # split-K clusters of more than 2 CTAs (hidden 2048)
     (37, 2048, 16, 16, 2, 1),    # clusters of more than 2 CTAs, ragged owned rows
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
-    (100, 1024, 8, 16, 1, 0),    # split-K clusters at hidden 1024 (16 k-steps)
+    (90, 1024, 8, 16, 1, 0),     # split-K clusters at hidden 1024 (16 k-steps)
+    (104, 4096, 32, 16, 1, 0),   # single CTAs, x box of the 104 live rows (rows past them stale)
     (129, 4096, 32, 16, 2, 1),   # CTA pairs (192-wide tiles), 72 + 57 token rows per pair
     (161, 4096, 32, 16, 1, 0),   # CTA pairs, 88 + 73 token rows (rows past them stale, not stored)
     (128, 4096, 32, 16, 1, 0),   # single CTAs, 128-wide tiles, one wave
@@ -254,7 +255,8 @@ def test_qkv_plan_splits_over_more_than_two_ctas(T, C):
 
 
 @pytest.mark.parametrize("T,C,kind", [
-    (1, 4096, 2), (64, 4096, 2), (96, 4096, 2), (120, 4096, 2), (100, 1024, 2), (128, 4096, 0), (129, 4096, 1),
+    (1, 4096, 2), (64, 4096, 2), (96, 4096, 2), (104, 4096, 0), (120, 4096, 0), (90, 1024, 2), (128, 4096, 0),
+    (129, 4096, 1),
     (256, 4096, 1), (200, 6400, 0), (300, 512, 0), (384, 4096, 0), (512, 4096, 1),
     (1000, 4096, 1), (8192, 4096, 1),
 ])
