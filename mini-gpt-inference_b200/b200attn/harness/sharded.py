@@ -62,9 +62,10 @@ def wait_statuses(store, world: int, timeout_s: float, tag: str = "") -> None:
     keys = [f"{_STATUS_PREFIX}{tag}/{r}" for r in range(world)]
     deadline = time.monotonic() + timeout_s
     missing = list(range(world))
-    # The poll interval starts at 0.5 ms and grows to 20 ms: ranks of a
+    # The poll interval starts at 0.5 ms and grows to 2 ms: ranks of a
     # balanced shard finish within a few ms of each other, and every ms one
-    # rank oversleeps here delays every rank's all-gather that follows.
+    # rank oversleeps here delays every rank's all-gather that follows (a
+    # store check costs one local round trip, far less than the pause).
     pause = 0.0005
     while missing and time.monotonic() < deadline:
         still = []
@@ -78,7 +79,7 @@ def wait_statuses(store, world: int, timeout_s: float, tag: str = "") -> None:
         missing = still
         if missing:
             time.sleep(pause)
-            pause = min(0.02, pause * 1.5)
+            pause = min(0.002, pause * 1.5)
     if missing:
         raise RuntimeError(f"ranks {missing} did not report within {timeout_s:.1f} s")
 
