@@ -12,15 +12,16 @@
 // token (attention.py:193-208 through KVBlockPool.write_layer) or by
 // index_put (attention.py:370-392).  A pool row (one token of one block, all
 // heads) is H * D = C contiguous elements, exactly the k (or v) third of an
-// output row, so the epilogue stores each 32-column run of a row straight
-// into the row's slot and k and v never exist as a separate tensor.
+// output row, so the epilogue stores each run of a row straight into the
+// row's slot and k and v never exist as a separate tensor.
 //
 // Three kernels share the warp roles below; qkv_plan picks one per call:
 //   CTA pairs   129+ tokens: 256 x BN tiles, tcgen05.mma.cta_group::2 (BN =
 //               192 up to 256 tokens, where it keeps more SMs busy, else 256);
 //   single CTA  128 x BN tiles (BN = 64 or 128) where those waves are
-//               cheaper than pair waves;
-//   split-K     decode-size token counts (<= 256): one output tile per
+//               cheaper than pair waves, and 97-128 tokens;
+//   split-K     decode-size token counts (<= 96, or <= 256 where the tiles
+//               above need more than one wave): one output tile per
 //               cluster, the reduction split over the cluster's CTAs.
 // The persistent ones (one CTA per SM) walk the output tiles in the grouped
 // order of tile_coords.  Warp roles (6 warps):
@@ -30,10 +31,13 @@
 //              N = BN, K = 16 per instruction (both operands K-major); two
 //              TMEM accumulators, so the epilogue of one tile overlaps the
 //              MMAs of the next;
-//   warps 2-5  epilogue: thread r owns output row r (TMEM lane r), reads 32
-//              columns at a time, rounds to bf16 (nearest even) and stores
-//              the 64-byte run to q_out or to the row's pool slot.
-// Rows past T and columns past 3C are zero-filled by TMA and not stored.
+//   warps 2-5  epilogue: thread r owns output row r (TMEM lane r), reads 64
+//              columns at a time and rounds them to bf16 (nearest even);
+//              the warp stores its 32 rows' 128-byte runs to q_out or to
+//              the rows' pool slots through shared staging rows (whole
+//              lines per store instruction).
+// Rows past T and columns past 3C are zero-filled by TMA (or, past the
+// x box of a short token tile, left stale) and not stored.
 // A slot outside [0, P*S) sets B200_DEV_BAD_SLOT and skips that row's k and
 // v (q is still written).  Every mbarrier wait is bounded; on a timeout the
 // CTA reports B200_DEV_WAIT_TIMEOUT, lets its own copies and MMAs finish,
