@@ -317,14 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
-      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
-        if (lane == 0) {
-          report(p.status, B200_DEV_WAIT_TIMEOUT);
-          *abort_v = 1;
-        }
-        break;
-      }
-      tc_fence_after();
+      // The row's destination (its slot is a global load) is resolved while
+      // the tile's MMAs still run.
       int mt, nt;
       tile_coords(t, p.m_tiles, p.n_tiles, kGroupRows / kBM, mt, nt);
       const int64_t row = static_cast<int64_t>(mt) * kBM + qd * 32 + lane;
@@ -340,6 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           report(p.status, B200_DEV_BAD_SLOT);
         }
       }
+      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
+        if (lane == 0) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          *abort_v = 1;
+        }
+        break;
+      }
+      tc_fence_after();
       const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
       // BN and n0 are multiples of 64: every batch lies in one of q, k, v.
 #pragma unroll 1
@@ -543,14 +545,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int t = pair; t < ntiles; t += npairs, ++i) {
       const int acc = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
-      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
-        if (lane == 0) {
-          report(p.status, B200_DEV_WAIT_TIMEOUT);
-          *abort_v = 1;
-        }
-        break;
-      }
-      tc_fence_after();
+      // The row's destination (its slot is a global load) is resolved while
+      // the tile's MMAs still run.
       int mt, nt;
       tile_coords(t, m_tiles, p.n_tiles, kGroupRows / (2 * kBM), mt, nt);
       const int lr = qd * 32 + lane;  // accumulator row (TMEM lane) of this CTA
@@ -566,6 +562,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           report(p.status, B200_DEV_BAD_SLOT);
         }
       }
+      if (!__all_sync(0xffffffffu, *abort_v == 0 && mbar_wait(&acc_full[acc], use & 1u))) {
+        if (lane == 0) {
+          report(p.status, B200_DEV_WAIT_TIMEOUT);
+          *abort_v = 1;
+        }
+        break;
+      }
+      tc_fence_after();
       const uint32_t tacc = tmem + lane_base + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 64)
