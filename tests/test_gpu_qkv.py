@@ -138,19 +138,28 @@ def test_qkv_kv_write_strided_x_int32_slots():
     _check_pool(c, y)
 
 
-def test_qkv_kv_write_bad_slots_are_flagged_and_skipped():
+@pytest.mark.parametrize("T,C,H", [
+    (40, 256, 8),      # split-K clusters
+    (104, 4096, 32),   # single CTAs, one short token tile
+    (300, 512, 4),     # single CTAs, several tiles per CTA
+    (160, 4096, 32),   # CTA pairs, 80 + 80 token rows
+    (1000, 4096, 32),  # CTA pairs, several token tiles
+])
+def test_qkv_kv_write_bad_slots_are_flagged_and_skipped(T, C, H):
+    """A slot outside the pool sets the status bit and skips that token's k
+    and v rows; its q row and every other token are still written."""
     from b200attn import _lib, qkv_kv_write_b200
 
-    c = _make(40, 256, 8, 16, 1, 0, seed=5)
+    c = _make(T, C, H, 16, 1, 0, seed=5 + T)
     c.slots[3] = -1
-    c.slots[17] = c.P * c.S  # one past the pool
+    c.slots[T - 5] = c.P * c.S  # one past the pool
     status = torch.zeros(1, dtype=torch.int32, device=_dev())
     with torch.inference_mode():
         q = qkv_kv_write_b200(c.x, c.w, c.pool, c.slots, 0, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) & _lib.DEV_BAD_SLOT
     y = _ref(c)
-    _assert_rounded(q.reshape(40, 256), y[:, :256], "q (all rows, bad slots included)")
+    _assert_rounded(q.reshape(T, C), y[:, :C], "q (all rows, bad slots included)")
     _check_pool(c, y)
 
 
