@@ -1234,25 +1234,40 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
   const int num_sms = dev.num_sms;
   const int64_t m_tiles = ceil_div(T, kBM);
   if (m_tiles <= 2 && T > 96) {
-    // 97..256 tokens: a tile per CTA (128 x 128) or per CTA pair (256 x
-    // BN) beats split-K clusters once those tiles fit in one wave: at
-    // hidden 4096 with every call on another layer's weights, 104-128 tokens
-    // take 24.2-24.3 us on single CTAs against 24.6-25.5 us split-K (96
-    // tokens: 24.1 against 24.3, level), and 256 tokens 27.0 us on 192-wide
-    // CTA pairs against 33 us.  Pairs take 192-wide tiles when those fit
-    // one wave too: more SMs, fewer bytes each.
-    const int64_t single_tiles = ceil_div(3 * C, 128);
-    if (m_tiles == 1 && single_tiles <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
-    if (m_tiles == 2 && ceil_div(3 * C, kPairBNNarrow) <= num_sms / 2)
+    // 97..256 tokens: a tile per CTA (128 x BN) or per CTA pair (256 x BN)
+    // beats split-K clusters.  Measured with every call on another layer's
+    // weights (CUDA graphs, one B200):
+    //  - hidden 4096: 104-128 tokens take 24.2-24.3 us on 128-wide single
+    //    CTAs against 24.6-25.5 us split-K (96 tokens: level), and 256
+    //    tokens 27.0 us on 192-wide pairs against 33 us;
+    //  - hidden 2048: 128 tokens take 11.9 us on 64-wide single CTAs (96
+    //    CTAs) against 12.8 us on 128-wide ones (48), and 192-256 tokens 13.0
+    //    us on 128-wide single CTAs (96) against 14.4 us on 192-wide pairs
+    //    (64 CTAs): with the tiles in one wave, more CTAs win;
+    //  - hidden 8192, 129-256 tokens: no layout fits one wave; persistent
+    //    192-wide pairs take 88-93 us, 256-wide ones 96-100 us and 128-wide
+    //    single CTAs 104-112 us.
+    const int64_t single64 = m_tiles * ceil_div(3 * C, 64);
+    const int64_t single128 = m_tiles * ceil_div(3 * C, 128);
+    const int64_t pairs192 = ceil_div(3 * C, kPairBNNarrow);
+    if (m_tiles == 1) {
+      if (single64 <= num_sms) return {QkvPlan::kSingle, 64, 1, kBM};
+      if (single128 <= num_sms) return {QkvPlan::kSingle, 128, 1, kBM};
+    } else {
+      if (single128 <= num_sms && single128 > 2 * pairs192) return {QkvPlan::kSingle, 128, 1, kBM};
+      if (pairs192 <= num_sms / 2) return {QkvPlan::kPair, kPairBNNarrow, 1, kBM};
+      if (ceil_div(3 * C, kPairBN) <= num_sms / 2) return {QkvPlan::kPair, kPairBN, 1, kBM};
       return {QkvPlan::kPair, kPairBNNarrow, 1, kBM};
-    if (m_tiles == 2 && ceil_div(3 * C, kPairBN) <= num_sms / 2)
-      return {QkvPlan::kPair, kPairBN, 1, kBM};
+    }
   }
   if (m_tiles <= 2) {
     // Few tokens (decode): the weights dominate and are read once, at a
     // per-SM rate that TMA caps.  Pick the tile width and reduction split
     // that stage the fewest bytes per CTA with every CTA resident at once
-    // (splits keep >= 8 chunks each).
+    // (splits keep >= 8 chunks each).  Each split past the first also costs
+    // its exchange and a shorter pipeline, counted as 6 x-rows per live row
+    // block: at hidden 2048, 96-wide tiles over 2 splits take 10.0-10.9 us
+    // at 1-96 tokens against 11.0-14.2 us for 192-wide tiles over 4.
     const int64_t k_iters = C / kBK;
     const int xrows = m_tiles == 1 ? static_cast<int>((T + 7) / 8 * 8) : kBM;
     QkvPlan best{QkvPlan::kSplit, 0, 0, 0};
@@ -1263,7 +1278,7 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev) {
         if (tiles * s > num_sms || (s > 1 && k_iters / s < 8)) continue;
         if (!split_fits(xrows, bn, s)) continue;
         if (s > 1 && tiles > split_capacity(s, dev)) continue;
-        const int64_t cost = ceil_div(k_iters, s) * (xrows + bn);
+        const int64_t cost = ceil_div(k_iters, s) * (xrows + bn) + (s - 1) * 6 * xrows;
         if (best_cost < 0 || cost < best_cost) {
           best = {QkvPlan::kSplit, bn, s, xrows};
           best_cost = cost;

@@ -75,8 +75,11 @@ def _check_pool(c, y, status_bits=0):
     (64, 4096, 32, 16, 1, 0),    # decode batch at H=32, D=128 (split-K clusters)
     (96, 4096, 32, 16, 1, 0),    # split-K clusters, 48 rows owned per cluster rank
     (77, 4096, 32, 16, 1, 0),    # split-K clusters, ragged owned rows (39 + 38)
-    (1, 2048, 16, 16, 1, 0),     # split-K clusters of more than 2 CTAs (hidden 2048)
-    (37, 2048, 16, 16, 2, 1),    # clusters of more than 2 CTAs, ragged owned rows
+    (1, 1664, 13, 16, 1, 0),     # split-K clusters of 3 CTAs (hidden 1664, 112-wide tiles)
+    (37, 3584, 28, 16, 2, 1),    # clusters of 3 CTAs, ragged owned rows (240-wide tiles)
+    (37, 2048, 16, 16, 1, 0),    # hidden 2048: 96-wide tiles over 2 splits
+    (128, 2048, 16, 16, 1, 0),   # hidden 2048: 64-wide single CTAs, one wave
+    (192, 2048, 16, 16, 1, 0),   # hidden 2048: 128-wide single CTAs, two token tiles, one wave
     (1, 4096, 32, 16, 1, 0),     # one token, split-K: most cluster ranks own no row
     (90, 1024, 8, 16, 1, 0),     # split-K clusters at hidden 1024 (16 k-steps)
     (104, 4096, 32, 16, 1, 0),   # single CTAs, x box of the 104 live rows (rows past them stale)
@@ -89,9 +92,9 @@ def _check_pool(c, y, status_bits=0):
     (600, 2048, 16, 16, 2, 1),   # CTA pairs; the second CTA of the last pair has no rows
     (77, 64, 1, 8, 1, 0),        # smallest hidden size: one k-step, ragged 128-wide tile
     (200, 192, 3, 32, 1, 0),     # three heads of 64, block size 32
-    (200, 3136, 49, 16, 1, 0),   # hidden 3136 (49 heads of 64): 49 pairs of 192-wide tiles
+    (200, 3136, 49, 16, 1, 0),   # hidden 3136 (49 heads of 64): 148 single-CTA tiles in one wave
     (200, 4160, 65, 16, 1, 0),   # CTA pairs, 192-wide tiles, 65 pairs
-    (200, 6400, 50, 16, 1, 0),   # more tiles than SMs: single CTAs, 128-wide tiles, 3 waves
+    (200, 6400, 50, 16, 1, 0),   # no layout in one wave: persistent CTA pairs, 100 tiles over 74 pairs
     (1000, 4160, 65, 16, 1, 0),  # CTA pairs, 3C = 48.75 tiles: ragged last output tile
 ])
 def test_qkv_kv_write_matches_fp32_projection(T, C, H, S, L, layer):
@@ -250,9 +253,9 @@ def test_qkv_kv_write_full_size_against_cublas():
     assert ((vf - yv).abs() <= yv.abs() * ulp + 1e-3).all()
 
 
-@pytest.mark.parametrize("T,C", [(1, 2048), (37, 2048)])
+@pytest.mark.parametrize("T,C", [(1, 1664), (37, 3584)])
 def test_qkv_plan_splits_over_more_than_two_ctas(T, C):
-    """The parity cases at hidden 2048 reach split-K clusters of 3+ CTAs."""
+    """The parity cases at hidden 1664 and 3584 reach split-K clusters of 3+ CTAs."""
     import ctypes
 
     from b200attn import _lib
@@ -265,8 +268,8 @@ def test_qkv_plan_splits_over_more_than_two_ctas(T, C):
 
 @pytest.mark.parametrize("T,C,kind", [
     (1, 4096, 2), (64, 4096, 2), (96, 4096, 2), (104, 4096, 0), (120, 4096, 0), (90, 1024, 2), (128, 4096, 0),
-    (129, 4096, 1),
-    (256, 4096, 1), (200, 6400, 0), (300, 512, 0), (384, 4096, 0), (512, 4096, 1),
+    (129, 4096, 1), (37, 2048, 2), (128, 2048, 0), (192, 2048, 0), (192, 8192, 1),
+    (256, 4096, 1), (200, 6400, 1), (300, 512, 0), (384, 4096, 0), (512, 4096, 1),
     (1000, 4096, 1), (8192, 4096, 1),
 ])
 def test_qkv_plan_covers_each_kernel(T, C, kind):
