@@ -19,9 +19,10 @@
 //   CTA pairs   129+ tokens: 256 x BN tiles, tcgen05.mma.cta_group::2 (BN =
 //               192 up to 256 tokens, where it keeps more SMs busy, else 256);
 //   single CTA  128 x BN tiles (BN = 64 or 128) where those waves are
-//               cheaper than pair waves, and 97-128 tokens;
-//   split-K     decode-size token counts (<= 96, or <= 256 where the tiles
-//               above need more than one wave): one output tile per
+//               cheaper than pair waves, and 97-256 tokens where one wave
+//               of them keeps more SMs busy than the pairs;
+//   split-K     decode-size token counts (<= 96, or <= 128 where single-CTA
+//               tiles need more than one wave): one output tile per
 //               cluster, the reduction split over the cluster's CTAs.
 // The persistent ones (one CTA per SM) walk the output tiles in the grouped
 // order of tile_coords.  Warp roles (6 warps):
