@@ -37,7 +37,6 @@ QkvPlan qkv_plan(int64_t T, int64_t C, const DeviceInfo& dev);
 int launch_bounded_wait_selftest(int32_t* status, int64_t limit_ns, cudaStream_t stream);
 
 // Split-K planning shared by the launcher and the workspace query.
-int64_t decode_tiles_per_split(int64_t units, int64_t max_tiles, int32_t hint, int num_sms);
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t D, int64_t M, int64_t S,
                               int32_t hint, size_t es, int num_sms);
 
