@@ -180,7 +180,11 @@ typedef struct {
  * bf16 pools with D in {64, 128} run on tcgen05 tensor cores (TMEM
  * accumulators, TMA-fed); f32 pools run the CUDA-core split-K kernel in
  * virtual-batch mode (exact fp32, TF32 never used) and need `workspace`
- * sized by b200_chunked_prefill_workspace_size().
+ * sized by b200_chunked_prefill_workspace_size().  A bf16 launch of fewer
+ * CTAs than about 85 % of the SMs (one sequence's chunk) splits each chunk's
+ * keys over several CTAs when `workspace` holds their partial rows (the same
+ * size query; batched calls use seqs[0]'s workspace and split only as far as
+ * it holds); without a workspace it runs unsplit, with the same results.
  */
 typedef struct {
   b200_kv_pool_t pool;

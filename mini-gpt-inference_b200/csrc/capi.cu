@@ -306,7 +306,9 @@ size_t b200_chunked_prefill_workspace_size(int64_t num_tokens, int64_t num_heads
   probe.pool.num_heads = num_heads;
   probe.pool.block_size = block_size;
   probe.num_tokens = num_tokens;
-  if (prefill_tc_supported(probe)) return 0;
+  if (prefill_tc_supported(probe))
+    return prefill_tc_workspace_bytes(num_tokens, num_heads, head_dim, block_table_len * block_size,
+                                      sm_count());
   return b200_paged_decode_workspace_size(num_tokens, num_heads, head_dim, block_table_len,
                                           block_size, kv_dtype, 0);
 }

@@ -20,6 +20,9 @@ int launch_kv_scatter(const b200_kv_scatter_args_t& a, cudaStream_t stream);
 // tcgen05 prefill over `n` sequences sharing one pool (bf16, D in {64,128}).
 int launch_prefill_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream);
 bool prefill_tc_supported(const b200_prefill_args_t& a);
+// Workspace for a key split over CTAs of one bf16 sequence's chunk (T tokens,
+// at most `keys` keys); 0 when its launch needs none.
+size_t prefill_tc_workspace_bytes(int64_t T, int64_t H, int64_t D, int64_t keys, int num_sms);
 // One warp waiting on an mbarrier nothing arrives on, with the given limit.
 // Fused QKV projection + KV write (tcgen05, bf16).  qkv_plan is the kernel
 // and tile shape it launches for T tokens of hidden size C: single CTAs with

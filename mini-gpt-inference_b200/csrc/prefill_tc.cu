@@ -31,6 +31,10 @@
 // V rows beyond the last valid key of the last tile are zeroed in smem
 // before the P.V MMA: unwritten pool rows can hold NaN and 0 * NaN is NaN
 // inside the tensor core as well (minivllm/paged_attention_batch.py:234-240).
+// Launches of few CTAs (one sequence's chunk) may split each query pair's
+// keys over CTAs (blockIdx.z): each writes its unnormalised rows with their
+// max and sum to the caller's workspace, and the last CTA to arrive, found
+// by an atomic counter (no spin-wait), combines them.
 // Every mbarrier wait is bounded; on a timeout the CTA reports
 // B200_DEV_WAIT_TIMEOUT, waits for its own MMAs and copies, frees TMEM and
 // exits.
@@ -93,6 +97,15 @@ struct PrefillParams {
   int32_t max_qtiles;
   int32_t* status;
   float scale_log2;
+  // Key split (ksplits > 1): CTA z of (item, head) covers the z-th of
+  // ksplits equal ranges of the item's key tiles and writes its unnormalised
+  // O rows with their (max, sum) to `part`; the last CTA to arrive (count)
+  // combines them.  part: [item][H][ksplits][D + 2][2 * kBM rows] fp32 (O
+  // by feature, then the row max and sum: a warp's 32 rows are contiguous);
+  // count: [item][H], zeroed before the launch.
+  int32_t ksplits;
+  float* part;
+  int32_t* count;
   SeqDesc seq[kMaxSeqs];
   // Work items, longest first: sequence | query pair << 8.  blockIdx.y picks
   // one, blockIdx.x is the head, so the CTAs with the most key tiles start
@@ -241,9 +254,28 @@ __device__ __forceinline__ void load_q_row(uint8_t* tile, int r, int i, int h, c
   }
 }
 
+// Key tiles [*j0, return value) that key split z of `splits` covers for
+// query tile w of the query pair starting at i0 (empty when j0 >= the
+// returned end): the pair's key tiles (those of its last query) are cut into
+// `splits` equal ranges, and each tile's own causal end clips them.
+__device__ __forceinline__ int key_split_range(const SeqDesc& sd, int i0, int w, int bn, int splits,
+                                               int z, int* j0) {
+  const int lo = i0 + w * kBM;
+  const int full = lo < sd.T ? static_cast<int>((sd.prefix + min(sd.T, lo + kBM) + bn - 1) / bn) : 0;
+  if (splits <= 1) {
+    *j0 = 0;
+    return full;
+  }
+  const int last = static_cast<int>((sd.prefix + min(sd.T, i0 + 2 * kBM) + bn - 1) / bn);
+  const int per = (last + splits - 1) / splits;
+  *j0 = z * per;
+  return max(*j0, min(full, *j0 + per));
+}
+
 // Per-CTA bookkeeping shared by the roles.
 struct Geom {
   int i0;          // first query of the CTA
+  int j0;          // first key tile of the CTA's range (key split), else 0
   int nkt[2];      // key tiles of query tile 0 / 1 (0 = tile inactive)
   int nmax;        // max(nkt): key tiles streamed through the rings
   int64_t total;   // keys any query of the CTA may see
@@ -280,11 +312,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   g.i0 = qp * 2 * kBM;
   if (g.i0 >= sd.T) return;
   const int64_t prefix = sd.prefix;
+  const int ksplit = static_cast<int>(blockIdx.z);
+  // Key tiles of query tile w (all keys up to its last query), clipped to
+  // this CTA's range under a key split; tile indices below stay relative to
+  // the range (ring stages and barrier phases start afresh in every CTA) and
+  // key positions add g.j0 back.
+  g.j0 = 0;
 #pragma unroll
   for (int w = 0; w < 2; ++w) {
-    const int lo = g.i0 + w * kBM;
-    const int hi = min(sd.T, lo + kBM);
-    g.nkt[w] = lo < sd.T ? static_cast<int>((prefix + hi + kBN - 1) / kBN) : 0;
+    const int j1 = key_split_range(sd, g.i0, w, kBN, p.ksplits, ksplit, &g.j0);
+    g.nkt[w] = j1 - g.j0;
   }
   g.nmax = max(g.nkt[0], g.nkt[1]);
   g.total = prefix + min(sd.T, g.i0 + 2 * kBM);
@@ -397,18 +434,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // is used, so the load's latency overlaps the wait and the copies.
     auto boxes = [&](int j) {
       return static_cast<int>(min(static_cast<int64_t>(boxes_per_tile),
-                                  (g.total - static_cast<int64_t>(j) * kBN + p.rbox - 1) >> p.rb_shift));
+                                  (g.total - static_cast<int64_t>(g.j0 + j) * kBN + p.rbox - 1) >> p.rb_shift));
     };
     auto entry = [&](int j) -> int64_t {
       if (j >= g.nmax || lane >= boxes(j) * L::HALVES) return 0;
-      const int64_t blk = (static_cast<int64_t>(j) * kBN + (static_cast<int64_t>(b) << p.rb_shift)) >> p.s_shift;
+      const int64_t blk = (static_cast<int64_t>(g.j0 + j) * kBN + (static_cast<int64_t>(b) << p.rb_shift)) >> p.s_shift;
       return blk < sd.table_len ? load_index(sd.table, blk * sd.ts, p.table_i64) : -1;
     };
     int64_t raw_next = entry(0);
     for (int j = 0; j < g.nmax; ++j) {
       const int st = j % NS;
       const uint32_t use = static_cast<uint32_t>(j / NS);
-      const int64_t key0 = static_cast<int64_t>(j) * kBN;
+      const int64_t key0 = static_cast<int64_t>(g.j0 + j) * kBN;
       const int nb = boxes(j);
       const bool mine = lane < nb * L::HALVES;
       const int64_t key = key0 + (static_cast<int64_t>(b) << p.rb_shift);
@@ -572,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t key0 = static_cast<int64_t>(j) * kBN;
+      const int64_t key0 = static_cast<int64_t>(g.j0 + j) * kBN;
       const bool need_mask = key0 + kBN - 1 > prefix + g.i0 + qt * kBM;  // some key may be masked
       float alpha = 1.f, m_use = m;
       bool rescale = false;
@@ -693,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the key split group 0 writes (O_0 2^(m_0-M) + O_1 2^(m_1-M)) /
     // (l_0 2^(m_0-M) + l_1 2^(m_1-M)), M = max(m_0, m_1).
     bool write = ok && nk > 0 && warp_live;
-    float a_self = 1.f, a_other = 0.f, inv = 0.f;
+    float a_self = 1.f, a_other = 0.f, inv = 0.f, m_row = m, l_row = l;
     if (g.split) {
       // Group 1 hands its row max and sum over through its S columns, free
       // once its last P.V has completed; group 0's thread r reads the same
@@ -713,14 +750,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         const float m1 = __uint_as_float(mb), l1 = __uint_as_float(lb);
         const float mm = fmaxf(m, m1);
-        a_self = ex2_approx(m - mm);
+        // (Under a key split over CTAs a row may see no key of this CTA's
+        // range at all: mm = -inf, and the row's partial is empty.)
+        a_self = m == -INFINITY ? 0.f : ex2_approx(m - mm);
         a_other = m1 == -INFINITY ? 0.f : ex2_approx(m1 - mm);
-        inv = 1.0f / (l * a_self + l1 * a_other);
+        m_row = mm;
+        l_row = l * a_self + l1 * a_other;
+        inv = 1.0f / l_row;
       }
     } else if (write) {
       inv = 1.0f / l;
     }
-    if (write) {
+    if (p.ksplits > 1) {
+      // Key split over CTAs: this CTA's unnormalised rows O (relative to the
+      // row max m_row) with (m_row, l_row) go to its slot; the last CTA of
+      // the (item, head) to arrive combines every split's rows.
+      const int64_t slot0 = (static_cast<int64_t>(blockIdx.y) * p.H + h) * p.ksplits;
+      constexpr int kRows = 2 * kBM;
+      constexpr int64_t kSlot = static_cast<int64_t>(D + 2) * kRows;
+      if (write) {
+        tc_fence_after();
+        float* prow = p.part + (slot0 + ksplit) * kSlot + qt * kBM + r;
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(tmem_o(w) + lane_base + c, o);
+          if (g.split) {
+            float o1[32];
+            tmem_ld32(tmem_o(1) + lane_base + c, o1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = o[e] * a_self + o1[e] * a_other;
+          } else {
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) prow[(c + e) * kRows] = o[e];
+        }
+        prow[D * kRows] = m_row;
+        prow[(D + 1) * kRows] = l_row;
+      }
+      // The ticket's outcome is shared through the word after the abort flag.
+      volatile int32_t* last_cta = reinterpret_cast<volatile int32_t*>(abort_flag) + 1;
+      __threadfence();
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (warp == 2 && lane == 0)
+        *last_cta = atomicAdd(&p.count[static_cast<int64_t>(blockIdx.y) * p.H + h], 1) == p.ksplits - 1;
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (*last_cta) {
+        __threadfence();
+        // Thread r of group w combines row r of query tile w over the splits
+        // whose range is not empty for that tile.
+        const int t = w;
+        const int iq_t = g.i0 + t * kBM + r;
+        if (iq_t < sd.T) {
+          auto row = [&](int z) { return p.part + (slot0 + z) * kSlot + t * kBM + r; };
+          // Splits whose range is empty for this tile wrote nothing for it.
+          uint32_t live_z = 0;
+          for (int z = 0; z < p.ksplits; ++z) {
+            int zj0;
+            if (key_split_range(sd, g.i0, t, kBN, p.ksplits, z, &zj0) > zj0) live_z |= 1u << z;
+          }
+          float M = -INFINITY;
+          for (uint32_t zs = live_z; zs; zs &= zs - 1) M = fmaxf(M, __ldcg(row(__ffs(zs) - 1) + D * kRows));
+          float L = 0.f;
+          for (uint32_t zs = live_z; zs; zs &= zs - 1) {
+            const float* src = row(__ffs(zs) - 1);
+            const float mz = __ldcg(src + D * kRows);
+            if (mz != -INFINITY) L += ex2_approx(mz - M) * __ldcg(src + (D + 1) * kRows);
+          }
+          const float linv = 1.0f / L;
+          const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            float o[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0.f;
+            for (uint32_t zs = live_z; zs; zs &= zs - 1) {
+              const float* src = row(__ffs(zs) - 1);
+              const float mz = __ldcg(src + D * kRows);
+              if (mz == -INFINITY) continue;
+              const float f = ex2_approx(mz - M) * linv;
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] += f * __ldcg(src + (c + e) * kRows);
+            }
+            const int64_t base = iq_t * sd.os0 + h * sd.os1 + c * sd.os2;
+            if (vec) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 8) {
+                const uint4 wv = make_uint4(pack_bf16(o[e], o[e + 1]), pack_bf16(o[e + 2], o[e + 3]),
+                                            pack_bf16(o[e + 4], o[e + 5]), pack_bf16(o[e + 6], o[e + 7]));
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(sd.out) + base + e) = wv;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) store_elem(sd.out, base + e * sd.os2, p.out_dtype, o[e]);
+            }
+          }
+        }
+      }
+    } else if (write) {
       tc_fence_after();
       const bool vec = p.out_vec && p.out_dtype == B200_DTYPE_BF16;
       const float ws = a_self * inv, wo = a_other * inv;
@@ -766,6 +895,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace
+
+namespace {
+
+// Key split over CTAs.  A launch of fewer CTAs than about 85 % of the SMs
+// (one CTA fits an SM) leaves the GPU mostly idle: one sequence's chunk of
+// 64 tokens over a 4032-token prefix at 32 heads is 32 CTAs, reading its KV
+// at 1.3 TB/s.  Its items' keys are then cut into ks ranges (>= 16 key
+// tiles each, so that a range outweighs its partial rows' write and
+// combine; ks <= 32), as many as the caller's workspace holds.
+constexpr int64_t kSplitRows = 2 * kBM;  // partial rows per (item, head, split)
+
+size_t split_workspace_bytes(int64_t items, int64_t H, int64_t ks, int64_t D) {
+  const size_t counters = (static_cast<size_t>(items * H) * sizeof(int32_t) + 255) & ~size_t(255);
+  return counters + static_cast<size_t>(items * H * ks * kSplitRows * (D + 2)) * sizeof(float);
+}
+
+int64_t plan_key_splits(int64_t items, int64_t H, int64_t key_tiles, int num_sms) {
+  const int64_t ctas = items * H;
+  if (ctas * 100 >= 85 * static_cast<int64_t>(num_sms)) return 1;
+  int64_t ks = ceil_div(85 * static_cast<int64_t>(num_sms), ctas * 100);
+  ks = std::min<int64_t>({ks, 32, key_tiles / 16});
+  return std::max<int64_t>(ks, 1);
+}
+
+}  // namespace
+
+size_t prefill_tc_workspace_bytes(int64_t T, int64_t H, int64_t D, int64_t keys, int num_sms) {
+  const int64_t bn = T <= kBM ? 128 : 64;
+  const int64_t items = ceil_div(T, 2 * kBM);
+  const int64_t ks = plan_key_splits(items, H, ceil_div(keys, bn), num_sms);
+  return ks > 1 ? split_workspace_bytes(items, H, ks, D) : 0;
+}
 
 bool prefill_tc_supported(const b200_prefill_args_t& a) {
   if (a.pool.dtype != B200_DTYPE_BF16) return false;
@@ -906,8 +1067,30 @@ int launch_tc(const b200_prefill_args_t* seqs, int64_t n, cudaStream_t stream,
                      [](const auto& a, const auto& b) { return a.first > b.first; });
     for (size_t w0 = 0; w0 < items.size(); w0 += kMaxWork) {
       const size_t nw = std::min<size_t>(kMaxWork, items.size() - w0);
-      for (size_t k = 0; k < nw; ++k) prm.work[k] = items[w0 + k].second;
-      const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw));
+      int64_t key_tiles = 0;  // the longest item's key tiles (those of its last query)
+      for (size_t k = 0; k < nw; ++k) {
+        const uint32_t it = items[w0 + k].second;
+        prm.work[k] = it;
+        const b200_prefill_args_t& s = seqs[base + (it & 0xFFu)];
+        const int64_t last_q = std::min<int64_t>(s.num_tokens, (static_cast<int64_t>(it >> 8) + 1) * 2 * kBM);
+        key_tiles = std::max<int64_t>(key_tiles, ceil_div(s.prefix_len + last_q, BN));
+      }
+      int64_t ks = a0.workspace != nullptr
+                       ? plan_key_splits(static_cast<int64_t>(nw), H, key_tiles, dev.num_sms)
+                       : 1;
+      while (ks > 1 && split_workspace_bytes(static_cast<int64_t>(nw), H, ks, D) > a0.workspace_bytes)
+        --ks;
+      prm.ksplits = static_cast<int32_t>(ks);
+      prm.count = nullptr;
+      prm.part = nullptr;
+      if (ks > 1) {
+        const size_t counters = static_cast<size_t>(nw * H) * sizeof(int32_t);
+        prm.count = static_cast<int32_t*>(a0.workspace);
+        prm.part = reinterpret_cast<float*>(static_cast<char*>(a0.workspace) + ((counters + 255) & ~size_t(255)));
+        cudaError_t e = cudaMemsetAsync(prm.count, 0, counters, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill split counters");
+      }
+      const dim3 grid(static_cast<unsigned>(H), static_cast<unsigned>(nw), static_cast<unsigned>(ks));
       prefill_tc_kernel<D_, BN><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "prefill_tc launch");

@@ -240,3 +240,42 @@ def test_prefill_long_prefix(prefix, T):
                                            prefix, 0, compute_dtype=torch.float64).float()
     err = (out.float().cpu() - want).abs().max().item()
     assert err <= 2e-2, f"max abs {err:.3e}"
+
+
+@pytest.mark.parametrize("prefix,T,heads", [(4032, 64, 32), (4032, 512, 32), (8000, 1, 8)])
+def test_prefill_key_split_over_ctas_matches_unsplit(prefix, T, heads):
+    """A launch of fewer CTAs than SMs (one sequence) splits each chunk's
+    keys over several CTAs when the caller's workspace holds their partial
+    rows, and the last CTA of each (query pair, head) combines them.  Its
+    output equals the unsplit launch's (the C ABI without a workspace) and
+    the float64 oracle's within the bf16 tolerance."""
+    import ctypes
+
+    from b200attn import _lib, chunked_prefill_b200, kv_scatter_b200, ops
+
+    c = cases.prefill_case(prefix, T, heads, 128, 16, 4100 + T, dtype=torch.bfloat16, n_layer=1,
+                           layer_idx=0)
+    d = _dev()
+    pool = c.pool.to(d)
+    kv_scatter_b200(c.k.to(d), c.v.to(d), pool, c.slots, 0)
+    lib = _lib.load()
+    table = ops._index_tensor(c.block_table, d, "block_table")
+    assert lib.b200_chunked_prefill_workspace_size(T, heads, 128, table.shape[0], 16,
+                                                   _lib.DTYPE_BF16) > 0  # the launch splits
+    status = torch.zeros(1, dtype=torch.int32, device=d)
+    q = c.q.to(d)
+    split = chunked_prefill_b200(q, pool, c.block_table, prefix, 0, status=status)
+    unsplit = torch.empty_like(split)
+    a = ops._prefill_struct(q, pool, ops._pool_struct(pool), table, prefix, 0, unsplit, status)
+    a.workspace = None
+    a.workspace_bytes = 0
+    _lib.check(lib.b200_chunked_prefill(ctypes.byref(a), ops._stream_ptr(d)), "prefill")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert (split.float() - unsplit.float()).abs().max().item() <= 2e-2
+    kp, vp = c.pool.k.clone(), c.pool.v.clone()
+    oracle.kv_scatter(kp, vp, c.k, c.v, c.slots, 0)
+    want = oracle.prefix_prefill_from_pool(c.q.float(), kp.float(), vp.float(), c.block_table,
+                                           prefix, 0, compute_dtype=torch.float64).float()
+    err = (split.float().cpu() - want).abs().max().item()
+    assert err <= 2e-2, f"max abs {err:.3e}"
