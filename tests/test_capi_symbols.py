@@ -131,6 +131,26 @@ def test_workspace_size_queries():
     assert big > 0
 
 
+def test_prefill_workspace_size_asks_for_a_key_split_only_when_the_launch_is_small():
+    """bf16 prefill: a launch of fewer CTAs than about 85 % of the SMs asks for a
+    workspace to split its keys over CTAs (>= 16 key tiles per split); a launch
+    with enough CTAs, or too few keys, asks for none."""
+    from b200attn import _lib
+
+    lib = _lib.load()
+    bf16 = _lib.DTYPE_BF16
+    # one sequence, chunk 64 over a 4032-token prefix at 32 heads: 32 CTAs, 32 key tiles
+    one = lib.b200_chunked_prefill_workspace_size(64, 32, 128, 256, 16, bf16)
+    assert one > 0
+    # chunk 2048 at 32 heads: 8 query pairs x 32 heads = 256 CTAs, no split
+    assert lib.b200_chunked_prefill_workspace_size(2048, 32, 128, 640, 16, bf16) == 0
+    # too few keys for two ranges of 16 tiles (700 tokens = 6 tiles of 128)
+    assert lib.b200_chunked_prefill_workspace_size(1, 8, 128, 44, 16, bf16) == 0
+    # more heads, fewer splits: the workspace never grows past 32 splits' rows
+    few = lib.b200_chunked_prefill_workspace_size(1, 1, 128, 4096, 16, bf16)
+    assert 0 < few <= 32 * 256 * 130 * 4 + 256
+
+
 def test_ops_reject_cpu_tensors_loudly():
     from b200attn import paged_attention_batch_b200
     import cases
