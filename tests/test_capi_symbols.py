@@ -131,6 +131,24 @@ def test_workspace_size_queries():
     assert big > 0
 
 
+def test_decode_split_plan_fills_one_wave_when_ctas_stay_short():
+    """bf16 decode at 32 heads of 128: the fewest splits that give about one wave
+    of CTAs while a CTA covers <= 8192 tokens (32 x 1024 tokens: 256 CTAs, no
+    split, no workspace); longer CTAs keep the two-wave rule (64 x 32768 tokens
+    splits)."""
+    from b200attn import _lib
+
+    lib = _lib.load()
+    bf16 = _lib.DTYPE_BF16
+    assert lib.b200_paged_decode_workspace_size(32, 32, 128, 64, 16, bf16, 0) == 0
+    assert lib.b200_paged_decode_workspace_size(1, 32, 128, 2048, 16, bf16, 0) > 0
+    assert lib.b200_paged_decode_workspace_size(64, 32, 128, 2048, 16, bf16, 0) > 0
+    # 8 x 4096 tokens takes 4 splits: its workspace holds 4 partial rows per head
+    w8 = lib.b200_paged_decode_workspace_size(8, 32, 128, 256, 16, bf16, 0)
+    w8_hint4 = lib.b200_paged_decode_workspace_size(8, 32, 128, 256, 16, bf16, 4)
+    assert w8 == w8_hint4 > 0
+
+
 def test_prefill_workspace_size_asks_for_a_key_split_only_when_the_launch_is_small():
     """bf16 prefill: a launch of fewer CTAs than about 85 % of the SMs asks for a
     workspace to split its keys over CTAs (>= 16 key tiles per split); a launch
